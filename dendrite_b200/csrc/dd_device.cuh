@@ -1,0 +1,232 @@
+// Device helpers shared by the sm_100a kernels: dtype conversions, mbarrier
+// and TMA wrappers (inline PTX), bounded waits with an error word.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp8.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "dd_internal.h"
+#include "dd_profile.h"
+
+namespace dd {
+
+// ---------------------------------------------------------------- error words
+// The first 256 bytes of every workspace hold device-side status words.
+enum DeviceError : uint32_t {
+  kDevErrNone = 0,
+  kDevErrBadPage = 1,      // page id >= num_pages in a device-side table
+  kDevErrWaitTimeout = 2,  // an mbarrier wait exceeded its time limit
+};
+struct WsHeader {
+  uint32_t error;      // first error code (DeviceError)
+  uint32_t error_aux;  // e.g. offending page id
+  uint32_t pad[62];
+};
+static_assert(sizeof(WsHeader) == kWsHeaderBytes, "workspace header");
+
+__device__ __forceinline__ void report_error(WsHeader* h, uint32_t code, uint32_t aux) {
+  if (h && atomicCAS(&h->error, 0u, code) == 0u) h->error_aux = aux;
+}
+
+// ---------------------------------------------------------------- conversions
+__device__ __forceinline__ float bf16_bits_to_float(uint16_t b) {
+  return __uint_as_float((uint32_t)b << 16);
+}
+
+// FP8 E4M3 code -> f32 (exact; the hardware conversion goes through f16).
+__device__ __forceinline__ float e4m3_to_float(uint8_t c) {
+  __half_raw h = __nv_cvt_fp8_to_halfraw((__nv_fp8_storage_t)c, __NV_E4M3);
+  return __half2float(__half(h));
+}
+
+// Two E4M3 codes (low byte first) -> two f32.
+__device__ __forceinline__ float2 e4m3x2_to_float2(uint16_t c2) {
+  __half2_raw h = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)c2, __NV_E4M3);
+  return __half22float2(__half2(h));
+}
+
+// f32 -> E4M3, round to nearest even, saturating to +-448 (NaN stays NaN).
+__device__ __forceinline__ uint8_t float_to_e4m3_satrn(float x) {
+  return (uint8_t)__nv_cvt_float_to_fp8(x, __NV_SATFINITE, __NV_E4M3);
+}
+
+// E8M0 shared exponent byte -> 2^(c-127) as f32 (c = 0 gives 2^-127, a
+// subnormal f32; c = 255 is NaN in the format and is never produced).
+__device__ __forceinline__ float e8m0_to_float(uint8_t c) {
+  if (c == 0) return __uint_as_float(0x00400000u);  // 2^-127
+  if (c == 255) return __uint_as_float(0x7fc00000u);
+  return __uint_as_float((uint32_t)c << 23);
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// ------------------------------------------------------------------- timing
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s: far above any legal wait
+
+// ------------------------------------------------------------------ mbarrier
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait: returns false (and sets *abort) if the phase does not
+// complete within kWaitLimitNs, or immediately if *abort is already set.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                          WsHeader* err) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 255u) == 0) {
+      if (*abort) return false;
+      if (global_ns() - t0 > kWaitLimitNs) {
+        *abort = 1;
+        report_error(err, kDevErrWaitTimeout, 0);
+        return false;
+      }
+    }
+  }
+}
+
+// ----------------------------------------------------------------------- TMA
+// 2-D tiled bulk tensor load global -> shared, completion on an mbarrier.
+// The innermost coordinate x is always 0 or a multiple of 64 elements here.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int32_t x, int32_t y,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+// 1-D bulk copy global -> shared (16-byte aligned addresses, size % 16 == 0).
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
+}
+
+// Named barrier among `nthreads` threads (multiple of 32).
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// ------------------------------------------------------------------- math
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+// Query head served by row j (0..g-1) of KV head k.
+__device__ __forceinline__ int qo_head_of(int gqa_map, int kv_head, int j, int Hkv, int g) {
+  return gqa_map == DD_GQA_TILED ? kv_head + j * Hkv : kv_head * g + j;
+}
+
+// Device description of where an item's rows read queries and write partial
+// states (shared by the attention kernels).
+struct AttnArgs {
+  const void* q;           // [B][Hq][D] bf16 or f32
+  const void* kv;          // page pool
+  const void* scales;      // per-head f32[2][Hkv] or E8M0 bytes
+  float* part_o;           // [slots][D]
+  float* part_lse;         // [slots], log2 domain
+  WsHeader* err;
+  const uint32_t* pages;   // plan page list (cascade) / page_indices (flat)
+  const int32_t* qorder;   // DFS position -> query (NULL: identity)
+  const WorkItem* items;   // cascade items (NULL: flat mode)
+  // flat mode
+  const int32_t* page_indptr;
+  const int32_t* num_tokens;
+  int32_t batch, nsplit, row_tiles;
+  // config
+  int32_t Hq, Hkv, g, D, kv_dtype, q_dtype, gqa_map, num_pages;
+  float scale_log2;        // softmax scale * log2(e)
+};
+
+// Resolve this CTA's work item. In flat mode the grid is
+// (nsplit, Hkv * row_tiles, batch) and each CTA takes a contiguous page range.
+__device__ __forceinline__ WorkItem resolve_item(const AttnArgs& a, const uint32_t*& pages,
+                                                 int row_tile_rows) {
+  WorkItem it;
+  if (a.items) {
+    it = a.items[blockIdx.x];
+    pages = a.pages + it.page_off;
+    return it;
+  }
+  const int s = blockIdx.x, b = blockIdx.z;
+  const int h = blockIdx.y / a.row_tiles, t = blockIdx.y % a.row_tiles;
+  const int ntok = a.num_tokens[b];
+  const int P = (ntok + kPageSize - 1) / kPageSize;
+  const int pb = (int)((int64_t)s * P / a.nsplit), pe = (int)((int64_t)(s + 1) * P / a.nsplit);
+  it.page_off = 0;
+  it.npages = pe - pb;
+  it.last_valid = (pe == P && (ntok % kPageSize)) ? ntok % kPageSize : kPageSize;
+  it.kv_head = h;
+  it.row0 = t * row_tile_rows;
+  it.nrows = min(row_tile_rows, a.g - it.row0);
+  it.q_begin = b;
+  it.slot_base = (s * a.batch + b) * a.Hq;
+  pages = a.pages + a.page_indptr[b] + pb;
+  return it;
+}
+
+// Inputs of the path merge (merge.cu). Path source: CSR (cascade plans) or
+// strided (flat split-K decode: slot (s * batch + p) * Hq for s < nsplit).
+struct MergeArgs {
+  const float* part_o;
+  const float* part_lse;
+  const int32_t* path_indptr;
+  const int32_t* path_slots;
+  int32_t nsplit;
+  const int32_t* qorder;
+  void* out;
+  float* lse;
+  int32_t batch, Hq, D, out_dtype;
+};
+
+}  // namespace dd

@@ -1,0 +1,397 @@
+// Host-side cascade planner: decode-batch block tables -> cascade plan.
+//
+// The reference builds no plan: ReferenceBackend::decode_batch loops over the
+// queries and re-gathers every block of every table
+// (crates/dendrite-core/src/attention/backend.rs:206-283), and the scheduler's
+// tree_state is dead (crates/dendrite-core/src/scheduler/mod.rs:31-33).
+// Shared prefixes are, however, literally shared physical block ids:
+// TreeState::fork clones the parent's BlockTable and bumps refcounts
+// (crates/dendrite-core/src/tree/state.rs:49-84,
+// crates/dendrite-core/src/cache/block_table.rs:97-103), and append allocates
+// fresh blocks for the child (state.rs:87-113, cache/pool.rs:76-97). The plan
+// is therefore the trie over the batch's block-id sequences, compressed into
+// runs ("nodes") that are each read by one contiguous range of queries in DFS
+// order. Every node is read once per KV head; its partial attention states are
+// merged along each query's root-to-leaf path.
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <unordered_map>
+
+#include "dd_internal.h"
+
+namespace dd {
+
+static thread_local std::string g_last_error;
+
+void set_error(const std::string& msg) { g_last_error = msg; }
+
+int fail(int code, const std::string& msg) {
+  set_error(msg);
+  return code;
+}
+
+int check_config(const dd_attn_config* cfg) {
+  if (!cfg) return fail(DD_ERR_INVALID_ARGUMENT, "config is NULL");
+  const int D = cfg->head_dim;
+  // Same rules as BatchDecodeKernel::new (batch_decode.rs:31-55).
+  if (D != 64 && D != 128 && D != 256)
+    return fail(DD_ERR_INVALID_ARGUMENT,
+                "unsupported head_dim: " + std::to_string(D) + ", supported: [64, 128, 256]");
+  if (cfg->num_qo_heads <= 0 || cfg->num_kv_heads <= 0)
+    return fail(DD_ERR_INVALID_ARGUMENT, "head counts must be positive");
+  if (cfg->num_qo_heads % cfg->num_kv_heads != 0)
+    return fail(DD_ERR_INVALID_ARGUMENT, "num_qo_heads must be divisible by num_kv_heads");
+  if (cfg->page_size != kPageSize)
+    return fail(DD_ERR_INVALID_ARGUMENT, "page_size must be 16");
+  if (cfg->num_pages < 0) return fail(DD_ERR_INVALID_ARGUMENT, "num_pages must be >= 0");
+  switch (cfg->kv_dtype) {
+    case DD_DTYPE_BF16: case DD_DTYPE_F32: case DD_DTYPE_E4M3: case DD_DTYPE_MXFP8: break;
+    case DD_DTYPE_F16: return fail(DD_ERR_NOT_AVAILABLE, "f16 KV pages are not implemented");
+    default: return fail(DD_ERR_INVALID_ARGUMENT, "unknown kv_dtype");
+  }
+  if (cfg->q_dtype != DD_DTYPE_BF16 && cfg->q_dtype != DD_DTYPE_F32)
+    return fail(cfg->q_dtype == DD_DTYPE_F16 ? DD_ERR_NOT_AVAILABLE : DD_ERR_INVALID_ARGUMENT,
+                "q_dtype must be bf16 or f32");
+  if (cfg->gqa_map != DD_GQA_TILED && cfg->gqa_map != DD_GQA_GROUPED)
+    return fail(DD_ERR_INVALID_ARGUMENT, "unknown gqa_map");
+  return DD_OK;
+}
+
+size_t plan_workspace_bytes(const dd_plan* p) {
+  const size_t D = (size_t)p->cfg.head_dim;
+  const size_t slots = (size_t)p->num_slots;
+  return kWsHeaderBytes + align_up(slots * D * sizeof(float), kAlign) +
+         align_up(slots * sizeof(float), kAlign);
+}
+
+// Which kernel family handles nodes with `rows` query rows per KV head.
+static int kind_for(const dd_attn_config& c, const dd_plan_options& o, int64_t rows);
+
+}  // namespace dd
+
+extern "C" int dd_tc_available(void);  // attn_tc.cu
+
+namespace dd {
+
+static int kind_for(const dd_attn_config& c, const dd_plan_options& o, int64_t rows) {
+  if (c.kv_dtype == DD_DTYPE_F32 || c.q_dtype != DD_DTYPE_BF16 || c.head_dim > 128)
+    return kItemSimple;
+  if (o.use_tensor_cores && rows >= 256 && c.head_dim == 128 && dd_tc_available())
+    return kItemTc;
+  return kItemMma;
+}
+
+static int row_tile_for(int kind) { return kind == kItemTc ? 128 : 64; }
+
+namespace {
+
+struct TrieKey {
+  int32_t parent;
+  uint32_t page;
+  int32_t valid;
+  bool operator==(const TrieKey& o) const {
+    return parent == o.parent && page == o.page && valid == o.valid;
+  }
+};
+struct TrieKeyHash {
+  size_t operator()(const TrieKey& k) const {
+    uint64_t h = (uint64_t)(uint32_t)k.parent * 0x9E3779B97F4A7C15ull;
+    h ^= ((uint64_t)k.page << 5 | (uint64_t)k.valid) + 0x632BE59BD9B4E019ull + (h << 6) + (h >> 2);
+    return (size_t)(h ^ (h >> 29));
+  }
+};
+struct TrieNode {
+  uint32_t page = 0;
+  int32_t valid = 0;
+  std::vector<int32_t> children;
+  std::vector<int32_t> ends;  // queries whose table ends here
+};
+
+}  // namespace
+
+// Builds nodes / pages / query_order from the tables.
+static int build_nodes(dd_plan* p, const int32_t* indptr, const uint32_t* ids,
+                       const int32_t* ntok) {
+  const int B = p->batch_size;
+  std::vector<int32_t> used(B);
+  for (int b = 0; b < B; ++b) {
+    const int nb = indptr[b + 1] - indptr[b];
+    if (nb < 0) return fail(DD_ERR_INVALID_ARGUMENT, "block_indptr must be non-decreasing");
+    if (ntok[b] < 0 || (int64_t)ntok[b] > (int64_t)nb * kPageSize)
+      return fail(DD_ERR_INVALID_ARGUMENT,
+                  "num_tokens[" + std::to_string(b) + "] exceeds its block table");
+    used[b] = (ntok[b] + kPageSize - 1) / kPageSize;
+    for (int i = 0; i < used[b]; ++i) {
+      const uint32_t id = ids[indptr[b] + i];
+      if ((int64_t)id >= (int64_t)p->cfg.num_pages)
+        // DendriteError::InvalidBlock (crates/dendrite-core/src/error.rs:15-17)
+        return fail(DD_ERR_INVALID_ARGUMENT, "invalid block id: " + std::to_string(id));
+    }
+    p->kv_tokens_flat += ntok[b];
+  }
+  auto valid_of = [&](int b, int i) {
+    return (i == used[b] - 1 && ntok[b] % kPageSize) ? ntok[b] % kPageSize : kPageSize;
+  };
+
+  if (!p->opts.share_prefixes) {
+    // Flat plan: one node per non-empty query, no sharing.
+    p->query_order.resize(B);
+    for (int b = 0; b < B; ++b) {
+      p->query_order[b] = b;
+      if (used[b] == 0) continue;
+      Node n;
+      n.q_begin = b;
+      n.num_q = 1;
+      n.num_tokens = ntok[b];
+      n.page_off = (int32_t)p->pages.size();
+      n.page_count = used[b];
+      n.last_valid = valid_of(b, used[b] - 1);
+      for (int i = 0; i < used[b]; ++i) p->pages.push_back(ids[indptr[b] + i]);
+      p->nodes.push_back(n);
+    }
+    p->max_depth = p->nodes.empty() ? 0 : 1;
+    return DD_OK;
+  }
+
+  // Trie over (page id, valid tokens) sequences. Node 0 is the empty root.
+  std::vector<TrieNode> trie(1);
+  std::unordered_map<TrieKey, int32_t, TrieKeyHash> index;
+  index.reserve((size_t)indptr[B] + 16);
+  for (int b = 0; b < B; ++b) {
+    int32_t cur = 0;
+    for (int i = 0; i < used[b]; ++i) {
+      TrieKey k{cur, ids[indptr[b] + i], valid_of(b, i)};
+      auto it = index.find(k);
+      if (it == index.end()) {
+        const int32_t nid = (int32_t)trie.size();
+        trie.emplace_back();
+        trie.back().page = k.page;
+        trie.back().valid = k.valid;
+        trie[cur].children.push_back(nid);
+        index.emplace(k, nid);
+        cur = nid;
+      } else {
+        cur = it->second;
+      }
+    }
+    trie[cur].ends.push_back(b);
+  }
+
+  // Iterative DFS that compresses single-child chains into nodes and emits
+  // queries in DFS order (queries ending at a trie node before its children).
+  p->query_order.reserve(B);
+  for (int32_t b : trie[0].ends) p->query_order.push_back(b);  // empty tables
+  struct Frame {
+    int32_t node;        // plan node index (-1 for the root)
+    int32_t trie_end;    // trie node where this plan node ends
+    size_t next_child;   // next child of trie_end to descend into
+  };
+  std::vector<Frame> stack;
+  stack.push_back({-1, 0, 0});
+  while (!stack.empty()) {
+    Frame& f = stack.back();
+    const TrieNode& tn = trie[f.trie_end];
+    if (f.next_child < tn.children.size()) {
+      const int32_t start = tn.children[f.next_child++];
+      Node n;
+      n.parent = f.node;
+      n.depth = f.node < 0 ? 0 : p->nodes[f.node].depth + 1;
+      n.q_begin = (int32_t)p->query_order.size();
+      n.page_off = (int32_t)p->pages.size();
+      int32_t t = start;
+      for (;;) {
+        p->pages.push_back(trie[t].page);
+        n.num_tokens += trie[t].valid;
+        n.last_valid = trie[t].valid;
+        if (trie[t].children.size() == 1 && trie[t].ends.empty()) t = trie[t].children[0];
+        else break;
+      }
+      n.page_count = (int32_t)p->pages.size() - n.page_off;
+      for (int32_t b : trie[t].ends) p->query_order.push_back(b);
+      p->nodes.push_back(n);
+      p->max_depth = std::max(p->max_depth, n.depth + 1);
+      stack.push_back({(int32_t)p->nodes.size() - 1, t, 0});
+    } else {
+      if (f.node >= 0) {
+        Node& n = p->nodes[f.node];
+        n.num_q = (int32_t)p->query_order.size() - n.q_begin;
+      }
+      stack.pop_back();
+    }
+  }
+  return DD_OK;
+}
+
+static void build_items(dd_plan* p) {
+  const dd_attn_config& c = p->cfg;
+  const int Hq = c.num_qo_heads, Hkv = c.num_kv_heads, g = Hq / Hkv, D = c.head_dim;
+  const double elem = c.kv_dtype == DD_DTYPE_F32 ? 4.0 : c.kv_dtype == DD_DTYPE_BF16 ? 2.0 : 1.0;
+  std::vector<std::vector<int32_t>> qslots(p->batch_size);
+  p->num_slots = 0;
+  for (const Node& n : p->nodes) {
+    p->kv_tokens += n.num_tokens;
+    const int64_t rows = (int64_t)n.num_q * g;
+    const int kind = kind_for(c, p->opts, rows);
+    const int rt = row_tile_for(kind);
+    const int64_t row_tiles = (rows + rt - 1) / rt;
+    // Split-K chunking. Each extra chunk costs one more partial state per
+    // (query, head) written and read back by the merge; allow at most 1/8 of
+    // the node's KV bytes for that.
+    const double kv_bytes = (double)n.page_count * 2 * Hkv * kPageSize * D * elem;
+    const double part_bytes = (double)n.num_q * Hq * (D + 1) * 4.0 * 2.0;
+    int64_t kmax = std::max<int64_t>(1, (int64_t)(kv_bytes / (8.0 * part_bytes)));
+    int64_t chunk_pages = p->opts.max_chunk_pages > 0 ? p->opts.max_chunk_pages
+                          : (row_tiles == 1 ? 16 : (int64_t)1 << 30);
+    int64_t k = std::min<int64_t>(kmax, (n.page_count + chunk_pages - 1) / chunk_pages);
+    k = std::max<int64_t>(1, std::min<int64_t>(k, n.page_count));
+    for (int64_t ci = 0; ci < k; ++ci) {
+      const int32_t pb = (int32_t)(ci * n.page_count / k);
+      const int32_t pe = (int32_t)((ci + 1) * n.page_count / k);
+      const int32_t slot_base = (int32_t)p->num_slots;
+      p->num_slots += (int64_t)n.num_q * Hq;
+      for (int32_t qi = 0; qi < n.num_q; ++qi)
+        qslots[n.q_begin + qi].push_back(slot_base + qi * Hq);
+      for (int h = 0; h < Hkv; ++h)
+        for (int64_t t = 0; t < row_tiles; ++t) {
+          WorkItem it;
+          it.page_off = n.page_off + pb;
+          it.npages = pe - pb;
+          it.last_valid = (pe == n.page_count) ? n.last_valid : kPageSize;
+          it.kv_head = h;
+          it.row0 = (int32_t)(t * rt);
+          it.nrows = (int32_t)std::min<int64_t>(rt, rows - t * rt);
+          it.q_begin = n.q_begin;
+          it.slot_base = slot_base;
+          p->items[kind].push_back(it);
+        }
+    }
+  }
+  // Longest items first so the big shared nodes start early (LPT order).
+  for (auto& v : p->items)
+    std::stable_sort(v.begin(), v.end(), [](const WorkItem& a, const WorkItem& b) {
+      return (int64_t)a.npages * a.nrows > (int64_t)b.npages * b.nrows;
+    });
+  p->path_indptr.assign(p->batch_size + 1, 0);
+  for (int i = 0; i < p->batch_size; ++i)
+    p->path_indptr[i + 1] = p->path_indptr[i] + (int32_t)qslots[i].size();
+  p->path_slots.reserve(p->path_indptr[p->batch_size]);
+  for (auto& v : qslots) p->path_slots.insert(p->path_slots.end(), v.begin(), v.end());
+}
+
+static void pack_image(dd_plan* p) {
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off = align_up(off + bytes, kAlign);
+    return o;
+  };
+  for (int k = 0; k < kNumItemKinds; ++k)
+    p->off_items[k] = take(p->items[k].size() * sizeof(WorkItem));
+  p->off_pages = take(p->pages.size() * sizeof(uint32_t));
+  p->off_qorder = take(p->query_order.size() * sizeof(int32_t));
+  p->off_pindptr = take(p->path_indptr.size() * sizeof(int32_t));
+  p->off_pslots = take(p->path_slots.size() * sizeof(int32_t));
+  p->image.assign(std::max<size_t>(off, kAlign), 0);
+  auto put = [&](size_t o, const void* src, size_t n) {
+    if (n) std::memcpy(p->image.data() + o, src, n);
+  };
+  for (int k = 0; k < kNumItemKinds; ++k)
+    put(p->off_items[k], p->items[k].data(), p->items[k].size() * sizeof(WorkItem));
+  put(p->off_pages, p->pages.data(), p->pages.size() * 4);
+  put(p->off_qorder, p->query_order.data(), p->query_order.size() * 4);
+  put(p->off_pindptr, p->path_indptr.data(), p->path_indptr.size() * 4);
+  put(p->off_pslots, p->path_slots.data(), p->path_slots.size() * 4);
+}
+
+}  // namespace dd
+
+using namespace dd;
+
+extern "C" {
+
+const char* dd_version(void) { return "dendrite_b200 0.1.0 (sm_100a)"; }
+
+const char* dd_last_error(void) { return g_last_error.c_str(); }
+
+int dd_validate_config(const dd_attn_config* cfg) { return check_config(cfg); }
+
+int dd_plan_create(const dd_attn_config* cfg, int32_t batch_size, const int32_t* block_indptr,
+                   const uint32_t* block_ids, const int32_t* num_tokens,
+                   const dd_plan_options* opts, dd_plan** out_plan) {
+  if (!out_plan) return fail(DD_ERR_INVALID_ARGUMENT, "out_plan is NULL");
+  *out_plan = nullptr;
+  int st = check_config(cfg);
+  if (st) return st;
+  if (batch_size < 0) return fail(DD_ERR_INVALID_ARGUMENT, "batch_size must be >= 0");
+  if (batch_size > 0 && (!block_indptr || !num_tokens))
+    return fail(DD_ERR_INVALID_ARGUMENT, "block_indptr / num_tokens is NULL");
+  if (batch_size > 0 && block_indptr[batch_size] > 0 && !block_ids)
+    return fail(DD_ERR_INVALID_ARGUMENT, "block_ids is NULL");
+  dd_plan* p = new (std::nothrow) dd_plan();
+  if (!p) return fail(DD_ERR_ALLOCATION, "host allocation failed");
+  p->cfg = *cfg;
+  if (p->cfg.scale <= 0.f) p->cfg.scale = 1.0f / std::sqrt((float)cfg->head_dim);
+  if (opts) {
+    p->opts = *opts;
+  } else {
+    p->opts = dd_plan_options{1, 0, 1, 0};
+  }
+  p->batch_size = batch_size;
+  try {
+    st = build_nodes(p, block_indptr, block_ids, num_tokens);
+    if (st) {
+      delete p;
+      return st;
+    }
+    build_items(p);
+    if (p->num_slots > INT32_MAX) {
+      delete p;
+      return fail(DD_ERR_INVALID_ARGUMENT, "plan too large (partial slots exceed 2^31)");
+    }
+    pack_image(p);
+  } catch (const std::bad_alloc&) {
+    delete p;
+    return fail(DD_ERR_ALLOCATION, "host allocation failed while planning");
+  }
+  *out_plan = p;
+  return DD_OK;
+}
+
+void dd_plan_destroy(dd_plan* plan) { delete plan; }
+
+int dd_plan_get_info(const dd_plan* p, dd_plan_info* info) {
+  if (!p || !info) return fail(DD_ERR_INVALID_ARGUMENT, "NULL argument");
+  info->batch_size = p->batch_size;
+  info->num_nodes = (int32_t)p->nodes.size();
+  int32_t n = 0;
+  for (auto& v : p->items) n += (int32_t)v.size();
+  info->num_items = n;
+  info->max_depth = p->max_depth;
+  info->kv_tokens = p->kv_tokens;
+  info->kv_tokens_flat = p->kv_tokens_flat;
+  info->workspace_bytes = plan_workspace_bytes(p);
+  info->device_bytes = p->image.size();
+  return DD_OK;
+}
+
+int dd_plan_export_nodes(const dd_plan* p, int32_t* parent, int32_t* q_begin, int32_t* num_q,
+                         int32_t* num_tokens, int32_t* page_offset, int32_t* page_count,
+                         uint32_t* pages, int32_t* query_order) {
+  if (!p) return fail(DD_ERR_INVALID_ARGUMENT, "plan is NULL");
+  for (size_t i = 0; i < p->nodes.size(); ++i) {
+    const Node& n = p->nodes[i];
+    if (parent) parent[i] = n.parent;
+    if (q_begin) q_begin[i] = n.q_begin;
+    if (num_q) num_q[i] = n.num_q;
+    if (num_tokens) num_tokens[i] = n.num_tokens;
+    if (page_offset) page_offset[i] = n.page_off;
+    if (page_count) page_count[i] = n.page_count;
+  }
+  if (pages && !p->pages.empty()) std::memcpy(pages, p->pages.data(), p->pages.size() * 4);
+  if (query_order && !p->query_order.empty())
+    std::memcpy(query_order, p->query_order.data(), p->query_order.size() * 4);
+  return DD_OK;
+}
+
+}  // extern "C"
