@@ -158,6 +158,7 @@ extern "C" int dd_decode_paged(const dd_attn_config* cfg, int32_t B, int32_t max
   int rc = check_config(cfg);
   if (rc) return rc;
   if (B < 0 || max_pages < 0) return fail(DD_ERR_INVALID_ARGUMENT, "bad batch size / max pages");
+  if (B > 65535) return fail(DD_ERR_INVALID_ARGUMENT, "batch_size > 65535: use a plan (dd_cascade_decode)");
   if (B == 0) return DD_OK;
   if (!page_indptr || !num_tokens || (!page_indices && max_pages > 0))
     return fail(DD_ERR_INVALID_ARGUMENT, "page table pointer is NULL");

@@ -284,8 +284,13 @@ __global__ void __launch_bounds__(kMmaThreads)
             o[n][2] *= al1;
             o[n][3] *= al1;
           }
-          const uint32_t pa[4] = {pack_bf16x2(p[0], p[1]), pack_bf16x2(p[4], p[5]),
-                                  pack_bf16x2(p[2], p[3]), pack_bf16x2(p[6], p[7])};
+          // P = P_hi + P_lo, both bf16: the two P.V products carry P to
+          // ~16 significant bits, so rounding P costs no accuracy.
+          uint32_t pa[4], pl[4];
+          split_bf16x2(p[0], p[1], pa[0], pl[0]);
+          split_bf16x2(p[4], p[5], pa[1], pl[1]);
+          split_bf16x2(p[2], p[3], pa[2], pl[2]);
+          split_bf16x2(p[6], p[7], pa[3], pl[3]);
           // O += P V.
 #pragma unroll
           for (int nn = 0; nn < D / 16; ++nn) {
@@ -295,6 +300,8 @@ __global__ void __launch_bounds__(kMmaThreads)
             ldsm_x4_t(vaddr + swz_bf16(t, chunk), b0, b1, b2, b3);
             mma_bf16(o[2 * nn], pa, b0, b1);
             mma_bf16(o[2 * nn + 1], pa, b2, b3);
+            mma_bf16(o[2 * nn], pl, b0, b1);
+            mma_bf16(o[2 * nn + 1], pl, b2, b3);
           }
         }
       }
@@ -384,7 +391,7 @@ int make_kv_tensor_map(CUtensorMap* map, const void* kv, int64_t num_pages, int 
   PFN_encodeTiled enc = get_encode_fn();
   if (!enc) return fail(DD_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   const uint64_t rows = (uint64_t)num_pages * 2 * Hkv * kPageSize;
-  if (rows == 0 || rows > 0xFFFFFFFFull)
+  if (rows == 0 || rows > 0x7FFFFFFFull)  // y coordinates are int32
     return fail(DD_ERR_INVALID_ARGUMENT, "page pool too large for a TMA descriptor");
   if (((uintptr_t)kv & 15) != 0) return fail(DD_ERR_INVALID_ARGUMENT, "kv_pages not 16-byte aligned");
   cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)rows};

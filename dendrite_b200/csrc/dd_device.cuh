@@ -66,6 +66,16 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
+// Two-term bf16 split of a pair: x = hi + lo with hi = bf16(x) and
+// lo = bf16(x - hi) (the subtraction is exact in f32).
+__device__ __forceinline__ void split_bf16x2(float a, float b, uint32_t& hi, uint32_t& lo) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  const float2 hf = __bfloat1622float2(h);
+  __nv_bfloat162 l = __floats2bfloat162_rn(a - hf.x, b - hf.y);
+  hi = *reinterpret_cast<uint32_t*>(&h);
+  lo = *reinterpret_cast<uint32_t*>(&l);
+}
+
 // ------------------------------------------------------------------- timing
 __device__ __forceinline__ uint64_t global_ns() {
   uint64_t t;

@@ -7,8 +7,8 @@ import dendrite_b200 as dd
 import oracle
 from dendrite_b200 import _lib
 from dendrite_b200 import workloads as wl
-from tests.helpers import (F32_MAX_ABS, F32_MEAN_REL, FP8_MAX_ABS, FP8_MEAN_REL, assert_close,
-                           bf16_bits, bits_to_f32, random_pool)
+from tests.helpers import (F32_MAX_ABS, F32_MEAN_REL, FP8_MAX_ABS_CAP, FP8_MEAN_REL_CAP,
+                           assert_close, bf16_bits, bits_to_f32, errors, random_pool)
 
 pytestmark = pytest.mark.gpu
 
@@ -131,8 +131,12 @@ def test_fp8_tree_vs_oracle(cuda, fmt):
     deq = oracle.dequantize(oc, os_, fmt, out="bf16")
     ref_fp8, _ = oracle_ref(tb, deq, bits_to_f32(q))
     assert_close(got, bits_to_f32(bf16_bits(ref_fp8)), what=f"{fmt} vs dequantised oracle")
+    # Against the bf16-KV oracle: the bound is 1.25x the error of the oracle's
+    # own FP8 path (FP8-dequant oracle vs bf16 oracle) on these inputs.
     ref_bf16, _ = oracle_ref(tb, pool, bits_to_f32(q))
-    assert_close(got, ref_bf16, FP8_MAX_ABS, FP8_MEAN_REL, f"{fmt} vs bf16 oracle")
+    oma, omr = errors(ref_fp8, ref_bf16)
+    assert oma <= FP8_MAX_ABS_CAP and omr <= FP8_MEAN_REL_CAP, (oma, omr)
+    assert_close(got, ref_bf16, 1.25 * oma, 1.25 * omr, f"{fmt} vs bf16 oracle")
 
 
 @pytest.mark.parametrize("kv", ["bf16", "f32", "e4m3"])
