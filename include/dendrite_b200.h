@@ -198,6 +198,27 @@ uint64_t dd_launch_count(void);
 void dd_profile_enable(int on);
 int dd_profile_read(double* ms, int64_t* launches, int32_t n);
 
+/* Paged batch decode that allocates nothing. No counterpart in the reference.
+ * For callers that cannot allocate device memory for scratch — a plugin that
+ * receives only input/output pointers from a host engine owning all device
+ * memory, or a decode loop that must not call cudaMalloc — this variant of
+ * dd_decode_paged takes no workspace: its scratch (split-K partial states and
+ * status words) lives in one static 4 MiB device array inside this library,
+ * held on every GPU that loads the library until the process exits. Arguments
+ * and results are dd_decode_paged's. A batch whose scratch
+ * (dd_decode_paged_workspace_size) exceeds 4 MiB is rejected with
+ * DD_ERR_WORKSPACE. The first call on a device looks up the array's device
+ * address (cudaGetSymbolAddress) with that device current; make that first
+ * call before any stream capture. Every call shares the one array, so calls
+ * whose executions overlap on the GPU (different streams, or different host
+ * threads on one device) race and corrupt each other's results: serialise
+ * them. The function calls no cudaMalloc / cudaFree. */
+int dd_decode_paged_static(const dd_attn_config* cfg, int32_t batch_size,
+                           int32_t max_pages_per_seq, const void* q, const void* kv_pages,
+                           const void* kv_scales, const int32_t* page_indptr,
+                           const int32_t* page_indices, const int32_t* num_tokens, void* out,
+                           float* lse, dd_stream_t stream);
+
 /* Merge of attention states: (o_a, lse_a) (+) (o_b, lse_b) -> (o, lse), f32,
  * natural-log LSE, element-wise over n rows of head_dim. The batched form of
  * merge_attention_outputs (crates/dendrite-ffi/src/flashinfer/cascade.rs:116-124).
