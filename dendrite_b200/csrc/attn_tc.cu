@@ -1,10 +1,392 @@
-// tcgen05 (TMEM-accumulator) path for cascade nodes with many query rows.
+// tcgen05 (5th-generation tensor core, TMEM accumulators) partial attention
+// for cascade nodes whose query rows form a dense contraction: the shared
+// root and upper nodes of a tree, where hundreds to thousands of (query, GQA
+// head) rows read the same pages.
+//
+// One CTA per work item = (node, KV head, 128-row tile, page range):
+//   warp 0      TMA producer: K and V tiles of 128 tokens (8 pages x 2 boxes
+//               of [16 tokens][64 dims], 128-byte swizzle) into a 4-slot ring;
+//   warp 1      allocates 384 TMEM columns; lane 0 issues every tcgen05.mma:
+//                 S_j = Q . K_j^T      (A = Q, B = K tile, both K-major smem)
+//                 O  += P_j . V_j      (A = P in TMEM, B = V tile MN-major)
+//               and signals completion with tcgen05.commit on mbarriers;
+//   warps 2-5   softmax: thread r owns query row r (= TMEM lane r), loads
+//               its S row, keeps the running max / sum in the log2 domain,
+//               writes P over the S columns as two bf16 terms (hi + lo, so
+//               the P.V product keeps ~16 significant bits of P), and
+//               rescales its O row in TMEM only when its max grows by more
+//               than 2^8 (otherwise exponentials use the stale max, exactly).
+// S is double-buffered in TMEM so Q.K_{j+1} runs while the softmax of tile j
+// does; P.V of tile j overlaps the softmax of tile j+1.
+//
+// The arithmetic is ReferenceBackend::decode's
+// (crates/dendrite-core/src/attention/backend.rs:254-262) over the node's
+// tokens; the normalised partial state goes to the workspace and is merged
+// along each query's path by merge.cu.
 #include "dd_device.cuh"
 
-extern "C" int dd_tc_available(void) { return 0; }
-
 namespace dd {
-int launch_attn_tc(const AttnArgs&, int64_t, int, cudaStream_t) {
-  return fail(DD_ERR_NOT_AVAILABLE, "tcgen05 path not built");
+
+constexpr int kTcRows = 128;
+constexpr int kTcTok = 128;             // tokens per tile
+constexpr int kTcSlots = 4;             // K/V ring slots (32 KiB each)
+constexpr int kTcThreads = 192;
+constexpr int kTcSlotBytes = kTcTok * 128 * 2;  // 128 tokens x 128 dims bf16
+constexpr int kTcQBytes = kTcRows * 128 * 2;
+constexpr int kTcSmem = kTcQBytes + kTcSlots * kTcSlotBytes + 1024;
+constexpr uint32_t kTmemCols = 512;     // power of two >= 384 (S0, S1, O)
+constexpr float kRescaleThreshold = 8.0f;  // log2 units
+
+// Instruction descriptor, kind::f16: D f32, A/B bf16, M = 128, N = 128.
+constexpr uint32_t kIdescQK = (1u << 4) | (1u << 7) | (1u << 10) | ((128u >> 3) << 17) |
+                              ((128u >> 4) << 24);
+constexpr uint32_t kIdescPV = kIdescQK | (1u << 16);  // B (V) is MN-major
+
+// Shared-memory matrix descriptor, 128-byte swizzle, sm_100 version bits.
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
 }
+
+__device__ __forceinline__ void umma_ss(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
+                                        uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+__device__ __forceinline__ void umma_ts(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t idesc,
+                                        uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc));
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// 32 lanes x 32 columns of 32-bit: thread i gets columns [col, col+32) of lane i.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+      "%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]),
+        "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]),
+        "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7]),
+      "f"(v[8]), "f"(v[9]), "f"(v[10]), "f"(v[11]), "f"(v[12]), "f"(v[13]), "f"(v[14]), "f"(v[15]),
+      "f"(v[16]), "f"(v[17]), "f"(v[18]), "f"(v[19]), "f"(v[20]), "f"(v[21]), "f"(v[22]), "f"(v[23]),
+      "f"(v[24]), "f"(v[25]), "f"(v[26]), "f"(v[27]), "f"(v[28]), "f"(v[29]), "f"(v[30]), "f"(v[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st16u(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+
+struct TcBars {
+  uint64_t kv_full[kTcSlots];
+  uint64_t kv_empty[kTcSlots];
+  uint64_t s_full[2];
+  uint64_t p_full[2];
+  uint64_t o_done;
+  uint64_t q_ready;
+  uint32_t tmem_base;
+  int abort;
+};
+
+__global__ void __launch_bounds__(kTcThreads, 1)
+    attn_tc_kernel(const __grid_constant__ CUtensorMap kv_map, AttnArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ TcBars bars;
+  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  uint8_t* q_s = smem;
+  uint8_t* slots = smem + kTcQBytes;
+
+  const WorkItem it = a.items[blockIdx.x];
+  const uint32_t* pages = a.pages + it.page_off;
+  const int npages = it.npages;
+  const int ntiles = (npages + 7) / 8;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kTcSlots; ++s) {
+      mbar_init(&bars.kv_full[s], 1);
+      mbar_init(&bars.kv_empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&bars.s_full[b], 1);
+      mbar_init(&bars.p_full[b], 128);
+    }
+    mbar_init(&bars.o_done, 1);
+    mbar_init(&bars.q_ready, 128);
+    bars.abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(&bars.tmem_base)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  if (threadIdx.x == 32 * 2) prefetch_tmap(&kv_map);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = bars.tmem_base;
+  volatile int* abort = &bars.abort;
+
+  if (warp == 0) {
+    // -------------------------------------------------------------- producer
+    if (lane == 0) {
+      const int64_t rows_total = (int64_t)a.num_pages * 2 * a.Hkv * kPageSize;
+      for (int idx = 0; idx < 2 * ntiles; ++idx) {
+        const int s = idx % kTcSlots;
+        if (idx >= kTcSlots &&
+            !mbar_wait(&bars.kv_empty[s], ((idx / kTcSlots) - 1) & 1, abort, a.err))
+          break;
+        const int j = idx >> 1, kv = idx & 1;
+        mbar_arrive_expect_tx(&bars.kv_full[s], kTcSlotBytes);
+        uint8_t* dst = slots + s * kTcSlotBytes;
+        for (int pj = 0; pj < 8; ++pj) {
+          const int pi = j * 8 + pj;
+          int y = (int)rows_total;  // past the end: TMA fills zeros
+          if (pi < npages) {
+            const uint32_t page = pages[pi];
+            if (page < (uint32_t)a.num_pages)
+              y = (int)((((int64_t)page * 2 + kv) * a.Hkv + it.kv_head) * kPageSize);
+            else
+              report_error(a.err, kDevErrBadPage, page);
+          }
+          tma_load_2d(dst + pj * 2048, &kv_map, 0, y, &bars.kv_full[s]);
+          tma_load_2d(dst + 16384 + pj * 2048, &kv_map, 64, y, &bars.kv_full[s]);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // --------------------------------------------------------- MMA issuer
+    if (lane == 0 && ntiles > 0) {
+      const uint32_t q_addr = smem_u32(q_s);
+      const uint32_t slot_addr = smem_u32(slots);
+      const uint32_t o_tmem = tbase + 256;
+      bool ok = mbar_wait(&bars.q_ready, 0, abort, a.err);
+      tc_fence_after();
+      auto issue_qk = [&](int j) -> bool {
+        const int s = (2 * j) % kTcSlots;
+        if (!mbar_wait(&bars.kv_full[s], ((2 * j) / kTcSlots) & 1, abort, a.err)) return false;
+        if (j >= 2 && !mbar_wait(&bars.o_done, (j - 2) & 1, abort, a.err)) return false;
+        tc_fence_after();
+        const uint32_t d = tbase + (uint32_t)(j & 1) * 128;
+        const uint32_t kb = slot_addr + s * kTcSlotBytes;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t off = (uint32_t)(kk >> 2) * 16384 + (uint32_t)(kk & 3) * 32;
+          umma_ss(d, umma_desc(q_addr + off, 16, 1024), umma_desc(kb + off, 16, 1024), kIdescQK,
+                  kk > 0);
+        }
+        umma_commit(&bars.s_full[j & 1]);
+        umma_commit(&bars.kv_empty[s]);
+        return true;
+      };
+      if (ok) ok = issue_qk(0);
+      for (int j = 0; ok && j < ntiles; ++j) {
+        if (j + 1 < ntiles && !issue_qk(j + 1)) break;
+        if (!mbar_wait(&bars.p_full[j & 1], (j >> 1) & 1, abort, a.err)) break;
+        const int s = (2 * j + 1) % kTcSlots;
+        if (!mbar_wait(&bars.kv_full[s], ((2 * j + 1) / kTcSlots) & 1, abort, a.err)) break;
+        tc_fence_after();
+        const uint32_t vb = slot_addr + s * kTcSlotBytes;
+        const uint32_t p_tmem = tbase + (uint32_t)(j & 1) * 128;
+#pragma unroll
+        for (int half = 0; half < 2; ++half)
+#pragma unroll
+          for (int kt = 0; kt < 8; ++kt)
+            umma_ts(o_tmem, p_tmem + half * 64 + kt * 8, umma_desc(vb + kt * 2048, 16384, 1024),
+                    kIdescPV, (j > 0 || half > 0 || kt > 0) ? 1u : 0u);
+        umma_commit(&bars.kv_empty[s]);
+        umma_commit(&bars.o_done);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------- softmax
+    const int quarter = warp & 3;           // TMEM lanes [32*quarter, +32)
+    const int r = quarter * 32 + lane;      // query row of this thread
+    const uint32_t lane_base = tbase + ((uint32_t)(quarter * 32) << 16);
+    // Q row r into the 128-byte-swizzled K-major tile.
+    {
+      const bool live = r < it.nrows;
+      const uint4* src = nullptr;
+      if (live) {
+        const int rr = it.row0 + r, qi = rr / a.g;
+        const int hq = qo_head_of(a.gqa_map, it.kv_head, rr % a.g, a.Hkv, a.g);
+        const int qid = a.qorder ? a.qorder[it.q_begin + qi] : it.q_begin + qi;
+        src = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(a.q) +
+                                             ((size_t)qid * a.Hq + hq) * 128);
+      }
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        const uint4 v = live ? src[c] : make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4*>(q_s + (c >> 3) * 16384 + r * 128 + (((c & 7) ^ (r & 7)) << 4)) = v;
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(&bars.q_ready);
+    }
+    float m_used = -INFINITY, l = 0.f;
+    for (int j = 0; j < ntiles; ++j) {
+      bool ok = mbar_wait(&bars.s_full[j & 1], (j >> 1) & 1, abort, a.err);
+      tc_fence_after();
+      const int valid = (j == ntiles - 1) ? (npages - 8 * j - 1) * kPageSize + it.last_valid : kTcTok;
+      const uint32_t sb = lane_base + (uint32_t)(j & 1) * 128;
+      float s[128];
+      {
+        float t[32];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          tmem_ld32(sb + c * 32, t);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) s[c * 32 + i] = t[i];
+        }
+      }
+      float mt = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 128; ++i) {
+        s[i] = (i < valid) ? s[i] * a.scale_log2 : -INFINITY;
+        mt = fmaxf(mt, s[i]);
+      }
+      if (!ok) mt = m_used;
+      // Warp-uniform decision (tcgen05.ld/st are warp-collective).
+      if (__any_sync(0xffffffffu, mt > m_used + kRescaleThreshold)) {
+        const float m_new = fmaxf(m_used, mt);
+        const float f = fast_exp2(m_used - m_new);  // 0 when m_used is -inf
+        if (j > 0) {
+          if (!mbar_wait(&bars.o_done, (j - 1) & 1, abort, a.err)) ok = false;
+          tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            float o[32];
+            tmem_ld32(lane_base + 256 + c * 32, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] *= f;
+            tmem_st32(lane_base + 256 + c * 32, o);
+          }
+        }
+        l *= f;
+        m_used = m_new;
+      }
+      float sum = 0.f;
+#pragma unroll
+      for (int i = 0; i < 128; ++i) {
+        s[i] = fast_exp2(s[i] - m_used);  // masked tokens: exp2(-inf) = 0
+        sum += s[i];
+      }
+      l += sum;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t hi[16], lo[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) split_bf16x2(s[c * 32 + 2 * i], s[c * 32 + 2 * i + 1], hi[i], lo[i]);
+        tmem_st16u(sb + c * 16, hi);
+        tmem_st16u(sb + 64 + c * 16, lo);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&bars.p_full[j & 1]);
+    }
+    // Epilogue: normalised O row and log2-domain LSE into the partial slot.
+    const bool live = r < it.nrows;
+    int64_t slot = 0;
+    if (live) {
+      const int rr = it.row0 + r, qi = rr / a.g;
+      const int hq = qo_head_of(a.gqa_map, it.kv_head, rr % a.g, a.Hkv, a.g);
+      slot = (int64_t)it.slot_base + (int64_t)qi * a.Hq + hq;
+    }
+    if (ntiles > 0) {
+      mbar_wait(&bars.o_done, (ntiles - 1) & 1, abort, a.err);
+      tc_fence_after();
+    }
+    const float inv = l > 0.f ? 1.f / l : 0.f;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      float o[32];
+      if (ntiles > 0) {
+        tmem_ld32(lane_base + 256 + c * 32, o);
+        tmem_wait_ld();
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[i] = 0.f;
+      }
+      if (live) {
+        float4* dst = reinterpret_cast<float4*>(a.part_o + slot * 128 + c * 32);
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          dst[i] = make_float4(o[4 * i] * inv, o[4 * i + 1] * inv, o[4 * i + 2] * inv, o[4 * i + 3] * inv);
+      }
+    }
+    if (live) a.part_lse[slot] = l > 0.f ? m_used + log2f(l) : -INFINITY;
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tbase), "r"(kTmemCols)
+                 : "memory");
+  }
+}
+
+int make_kv_tensor_map(CUtensorMap* map, const void* kv, int64_t num_pages, int Hkv, int D,
+                       int elem_bytes);
+
+int launch_attn_tc(const AttnArgs& a, int64_t num_pages, int num_items, cudaStream_t st) {
+  if (a.D != 128 || a.kv_dtype != DD_DTYPE_BF16 || a.q_dtype != DD_DTYPE_BF16)
+    return fail(DD_ERR_NOT_AVAILABLE, "tcgen05 path: bf16 KV and queries, head_dim 128");
+  CUtensorMap map;
+  int rc = make_kv_tensor_map(&map, a.kv, num_pages, a.Hkv, a.D, 2);
+  if (rc) return rc;
+  cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       kTcSmem);
+  if (e != cudaSuccess) return fail(DD_ERR_CUDA, std::string("attn_tc attribute: ") + cudaGetErrorString(e));
+  {
+    ProfScope ps(kProfTc, st);
+    attn_tc_kernel<<<num_items, kTcThreads, kTcSmem, st>>>(map, a);
+  }
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(DD_ERR_CUDA, std::string("attn_tc launch: ") + cudaGetErrorString(e));
+  return DD_OK;
+}
+
 }  // namespace dd
+
+extern "C" int dd_tc_available(void) { return 1; }

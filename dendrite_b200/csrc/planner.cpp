@@ -77,7 +77,8 @@ namespace dd {
 static int kind_for(const dd_attn_config& c, const dd_plan_options& o, int64_t rows) {
   if (c.kv_dtype == DD_DTYPE_F32 || c.q_dtype != DD_DTYPE_BF16 || c.head_dim > 128)
     return kItemSimple;
-  if (o.use_tensor_cores && rows >= 256 && c.head_dim == 128 && dd_tc_available())
+  if (o.use_tensor_cores && rows >= 128 && c.head_dim == 128 && c.kv_dtype == DD_DTYPE_BF16 &&
+      dd_tc_available())
     return kItemTc;
   return kItemMma;
 }

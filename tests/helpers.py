@@ -14,8 +14,10 @@ MAX_ABS = 2e-2
 MEAN_REL = 1e-3
 F32_MAX_ABS = 1e-4
 F32_MEAN_REL = 1e-5
-FP8_MAX_ABS_CAP = 4.0
-FP8_MEAN_REL_CAP = 0.1
+# Sanity caps on the oracle's own FP8 error (x50 outliers in K and V make
+# per-head E4M3 / MXFP8 coarse; these only catch a broken codec).
+FP8_MAX_ABS_CAP = 20.0
+FP8_MEAN_REL_CAP = 0.15
 
 
 def bf16_bits(x: np.ndarray) -> np.ndarray:

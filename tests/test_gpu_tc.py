@@ -1,0 +1,135 @@
+"""GPU parity of the tcgen05 kernel (wide shared nodes) against the oracle."""
+import numpy as np
+import pytest
+import torch
+
+import dendrite_b200 as dd
+import oracle
+from dendrite_b200 import _lib
+from dendrite_b200 import workloads as wl
+from tests.helpers import assert_close, bf16_bits, bits_to_f32, random_pool
+
+pytestmark = pytest.mark.gpu
+
+
+def _dev_bf16(bits, dev):
+    return torch.from_numpy(bits.view(np.int16).copy()).view(torch.bfloat16).to(dev)
+
+
+def _run(tb, pool_bits, q_bits, dev, tc=True, gqa=0):
+    cfg = dd.make_config(tb.num_qo_heads, tb.num_kv_heads, tb.head_dim, tb.num_pages, gqa_map=gqa)
+    plan = dd.CascadePlan(cfg, tb.indptr, tb.block_ids, tb.num_tokens, use_tensor_cores=tc)
+    plan.upload(dev)
+    launches = _lib.launch_count()
+    _lib.profile_enable(True)
+    out, lse = dd.cascade_decode(cfg, plan, _dev_bf16(q_bits, dev), _dev_bf16(pool_bits, dev))
+    torch.cuda.synchronize()
+    prof = _lib.profile_read()
+    _lib.profile_enable(False)
+    return out.float().cpu().numpy(), lse.cpu().numpy(), prof, _lib.launch_count() - launches
+
+
+def _groups(groups, seed):
+    """Queries in groups sharing one whole table each: [(n_queries, tokens)]."""
+    rng = np.random.default_rng(seed)
+    ids, indptr, ntok, nxt = [], [0], [], 0
+    for nq, tok in groups:
+        nb = -(-tok // 16)
+        tab = list(range(nxt, nxt + nb))
+        nxt += nb
+        for _ in range(nq):
+            ids += tab
+            indptr.append(len(ids))
+            ntok.append(tok)
+    perm = rng.permutation(nxt).astype(np.uint32)
+    return np.array(indptr, np.int32), perm[np.array(ids, np.int64)], np.array(ntok, np.int32), nxt
+
+
+class _TB:
+    def __init__(self, Hq, Hkv, D, indptr, ids, ntok, P):
+        self.num_qo_heads, self.num_kv_heads, self.head_dim = Hq, Hkv, D
+        self.indptr, self.block_ids, self.num_tokens, self.num_pages = indptr, ids, ntok, P
+        self.batch_size = len(ntok)
+
+
+CASES = [
+    # (Hq, Hkv, prefix, leaves, suffix range, gqa)
+    (32, 8, 1008, 37, (1, 40), 0),     # 148 root rows: tiles of 128 + 20; 63 pages
+    (32, 8, 2048, 64, (16, 200), 1),   # grouped GQA, 256 rows
+    (64, 8, 4096, 64, (1, 300), 0),    # g = 8, 512 rows, 32 token tiles
+    (32, 4, 496, 40, (1, 17), 0),      # 320 rows over 31 pages (one partial tile)
+]
+
+
+@pytest.mark.parametrize("Hq,Hkv,prefix,leaves,suffix,gqa", CASES)
+def test_wide_root_vs_oracle(cuda, Hq, Hkv, prefix, leaves, suffix, gqa):
+    seed = Hq + prefix + leaves
+    tb = wl.build_tree("wide", Hq, Hkv, 128, prefix, [], leaves, suffix, seed)
+    rng = np.random.default_rng(seed)
+    pool = bf16_bits(random_pool(rng, tb.num_pages, Hkv, 128))
+    q = bf16_bits(rng.standard_normal((tb.batch_size, Hq, 128)).astype(np.float32))
+    got, lse, prof, _ = _run(tb, pool, q, cuda, gqa=gqa)
+    assert prof["attn_tc"][1] == 1, prof  # the wide root went through tcgen05
+    ref, ref_lse = oracle.decode_batch(bits_to_f32(q), pool, tb.indptr, tb.block_ids,
+                                       tb.num_tokens, Hkv, gqa_grouped=bool(gqa))
+    assert_close(got, bits_to_f32(bf16_bits(ref)), what="tc root")
+    np.testing.assert_allclose(lse, ref_lse, atol=2e-3)
+
+
+def test_shared_partial_last_page_through_tc(cuda):
+    indptr, ids, ntok, P = _groups([(40, 1000), (1, 37), (33, 129)], 3)
+    tb = _TB(32, 8, 128, indptr, ids, ntok, P)
+    rng = np.random.default_rng(3)
+    pool = bf16_bits(random_pool(rng, P, 8, 128))
+    q = bf16_bits(rng.standard_normal((len(ntok), 32, 128)).astype(np.float32))
+    got, lse, prof, _ = _run(tb, pool, q, cuda)
+    assert prof["attn_tc"][1] == 1
+    ref, ref_lse = oracle.decode_batch(bits_to_f32(q), pool, indptr, ids, ntok, 8)
+    assert_close(got, bits_to_f32(bf16_bits(ref)), what="partial pages")
+    np.testing.assert_allclose(lse, ref_lse, atol=2e-3)
+
+
+def test_tc_matches_mma_path(cuda):
+    tb = wl.build_tree("cmp", 32, 8, 128, 3072, [(4, 128, 512)], 16, (1, 100), 9)
+    rng = np.random.default_rng(9)
+    pool = bf16_bits(random_pool(rng, tb.num_pages, 8, 128))
+    q = bf16_bits(rng.standard_normal((tb.batch_size, 32, 128)).astype(np.float32))
+    a, la, pa, _ = _run(tb, pool, q, cuda, tc=True)
+    b, lb, pb, _ = _run(tb, pool, q, cuda, tc=False)
+    assert pa["attn_tc"][1] == 1 and pb["attn_tc"][1] == 0
+    assert_close(a, b, what="tc vs mma")
+    np.testing.assert_allclose(la, lb, atol=1e-3)
+
+
+def test_large_score_range_rescales(cuda):
+    """Keys whose scores grow along the sequence force the lazy O rescale."""
+    indptr, ids, ntok, P = _groups([(48, 2048)], 4)
+    tb = _TB(32, 8, 128, indptr, ids, ntok, P)
+    rng = np.random.default_rng(4)
+    x = random_pool(rng, P, 8, 128)
+    # page order along the sequence gets a growing key scale: scores climb by
+    # far more than 2^8 across tiles
+    order = ids[:ntok[0] // 16 + 1]
+    for i, p in enumerate(order):
+        x[p, 0] *= 1.0 + 0.15 * i
+    pool = bf16_bits(x)
+    q = bf16_bits(rng.standard_normal((len(ntok), 32, 128)).astype(np.float32))
+    got, lse, prof, _ = _run(tb, pool, q, cuda)
+    assert prof["attn_tc"][1] == 1
+    ref, ref_lse = oracle.decode_batch(bits_to_f32(q), pool, indptr, ids, ntok, 8)
+    assert_close(got, bits_to_f32(bf16_bits(ref)), what="rescale")
+    np.testing.assert_allclose(lse, ref_lse, rtol=1e-4, atol=1e-2)
+
+
+def test_mcts_subset_vs_oracle(cuda):
+    """A 128-leaf version of the MCTS tree (root through tcgen05), all queries."""
+    tb = wl.build_tree("mcts128", 32, 8, 128, 8192, [(4, 128, 1024), (4, 128, 1024), (2, 128, 1024)],
+                       4, (16, 256), 0xD3D1)
+    rng = np.random.default_rng(1)
+    pool = bf16_bits(random_pool(rng, tb.num_pages, 8, 128))
+    q = bf16_bits(rng.standard_normal((tb.batch_size, 32, 128)).astype(np.float32))
+    got, lse, prof, n = _run(tb, pool, q, cuda)
+    assert prof["attn_tc"][1] == 1 and n >= 3
+    ref, ref_lse = oracle.decode_batch(bits_to_f32(q), pool, tb.indptr, tb.block_ids, tb.num_tokens, 8)
+    assert_close(got, bits_to_f32(bf16_bits(ref)), what="mcts128")
+    np.testing.assert_allclose(lse, ref_lse, atol=2e-3)
