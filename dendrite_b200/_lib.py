@@ -120,7 +120,7 @@ PROFILE_KINDS = ("attn_simple", "attn_mma", "attn_tc", "merge", "quant", "other"
 def _load() -> C.CDLL:
     if not _LIB_PATH.exists():
         raise ImportError(
-            f"{_LIB_PATH.name} is not built: run `python -m dendrite_b200.build` "
+            f"{_LIB_PATH.name} is not built: run `python dendrite_b200/build.py` "
             "(the CUDA extension is required; there is no CPU fallback)")
     lib = C.CDLL(str(_LIB_PATH))
     for name, (res, args) in SIGNATURES.items():
