@@ -7,9 +7,13 @@ so no CPU path can stand in for the CUDA kernels.
 from __future__ import annotations
 
 import ctypes as C
+import os
 from pathlib import Path
 
-_LIB_PATH = Path(__file__).resolve().parent / "libdendrite_b200.so"
+# DENDRITE_B200_LIB may point at another build of the same library (e.g. one
+# compiled with different flags for an experiment).
+_LIB_PATH = Path(os.environ.get("DENDRITE_B200_LIB") or
+                 Path(__file__).resolve().parent / "libdendrite_b200.so")
 
 # dd_status -> exception class; mirrors FfiError (crates/dendrite-ffi/src/error.rs:9-30).
 DD_OK = 0

@@ -9,7 +9,7 @@
 
 namespace dd {
 cudaError_t launch_attn_simple(const AttnArgs& a, dim3 grid, cudaStream_t st);
-int launch_attn_mma(const AttnArgs& a, int64_t num_pages, dim3 grid, cudaStream_t st);
+int launch_attn_mma(const AttnArgs& a, int64_t num_pages, cudaStream_t st);
 bool mma_supported(int D, int kv_dtype);
 int launch_attn_tc(const AttnArgs& a, int64_t num_pages, int num_items, cudaStream_t st);
 cudaError_t launch_merge(const MergeArgs& a, cudaStream_t st);
@@ -48,8 +48,8 @@ static int check_kv_ptrs(const dd_attn_config* c, const void* q, const void* kv,
   if (!kv && c->num_pages > 0) return fail(DD_ERR_INVALID_ARGUMENT, "kv_pages is NULL");
   if ((c->kv_dtype == DD_DTYPE_E4M3 || c->kv_dtype == DD_DTYPE_MXFP8) && !scales)
     return fail(DD_ERR_INVALID_ARGUMENT, "FP8 KV pages need kv_scales");
-  if (((uintptr_t)kv & 15) || ((uintptr_t)q & 3))
-    return fail(DD_ERR_INVALID_ARGUMENT, "kv_pages must be 16-byte and q 4-byte aligned");
+  if (((uintptr_t)kv & 15) || ((uintptr_t)q & 15))
+    return fail(DD_ERR_INVALID_ARGUMENT, "kv_pages and q must be 16-byte aligned");
   return DD_OK;
 }
 
@@ -116,7 +116,8 @@ extern "C" int dd_cascade_decode(const dd_attn_config* cfg, const dd_plan* p, co
       e = launch_attn_simple(a, dim3(n), st);
       if (e != cudaSuccess) return cuda_fail(e, "attn_simple launch");
     } else if (k == kItemMma) {
-      rc = launch_attn_mma(a, cfg->num_pages, dim3(n), st);
+      a.num_items = n;
+      rc = launch_attn_mma(a, cfg->num_pages, st);
       if (rc) return rc;
     } else {
       rc = launch_attn_tc(a, cfg->num_pages, n, st);
@@ -178,10 +179,11 @@ extern "C" int dd_decode_paged(const dd_attn_config* cfg, int32_t B, int32_t max
   a.batch = B;
   a.nsplit = ns;
   const bool mma = cfg->q_dtype == DD_DTYPE_BF16 && mma_supported(cfg->head_dim, cfg->kv_dtype);
-  a.row_tiles = (a.g + 63) / 64;
+  a.row_tiles = mma ? (a.g + 15) / 16 : (a.g + 63) / 64;
   const dim3 grid(ns, cfg->num_kv_heads * a.row_tiles, B);
   if (mma) {
-    rc = launch_attn_mma(a, cfg->num_pages, grid, st);
+    a.num_items = ns * cfg->num_kv_heads * a.row_tiles * B;
+    rc = launch_attn_mma(a, cfg->num_pages, st);
     if (rc) return rc;
   } else {
     e = launch_attn_simple(a, grid, st);

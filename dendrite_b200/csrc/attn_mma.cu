@@ -1,31 +1,42 @@
-// Paged partial attention for cascade nodes with up to 64 query rows per KV
-// head (leaves, deep shared nodes, flat batch decode), bf16 / E4M3 / MXFP8 KV.
+// Paged partial attention for cascade nodes with up to 16 query rows per
+// work item (leaves, deep shared nodes, flat batch decode; wider nodes are
+// cut into 16-row items), bf16 / E4M3 / MXFP8 KV.
 //
-// Structure (one CTA per work item, 4 consumer warps + 1 producer warp):
-//  - the producer lane streams the item's pages through a ring of shared
-//    memory stages with TMA (cp.async.bulk.tensor, 128-byte swizzle) — four
-//    16-token pages of K and V per stage, each page slice [16][head_dim]
-//    contiguous in the pool — completion tracked by mbarriers;
-//  - FP8 pages land as 1-byte codes (+ E8M0 bytes for MXFP8) and the consumer
-//    warps dequantise them to bf16 in shared memory (code * scale, rounded to
-//    bf16), so the HBM stream stays 1 byte per element;
-//  - each consumer warp owns 16 query rows (a GQA group of one or more
-//    queries that share the node) and a subset of the stage's pages, runs
-//    q.k^T and p.v as m16n8k16 bf16 tensor-core tiles with f32 accumulators,
-//    and keeps an online softmax (running max / sum in the log2 domain);
-//  - warps that split the pages of a node combine their states through shared
-//    memory; the CTA writes one normalised partial state per row.
+// Persistent, multi-stream kernel. One CTA per SM holds kStreams independent
+// streams; each stream is one consumer warp with its own ring of shared-
+// memory stages. Work items are claimed from a device counter (items are
+// sorted longest first), one item at a time per stream.
+//  - One producer warp serves all streams: lane c drives stream c. For the
+//    stream's current item it claims work, reads page ids a stage ahead, and
+//    fills free stages with TMA (cp.async.bulk.tensor): one box per 16-token
+//    page slice of K or of V ([16][head_dim] contiguous in the pool, 128-byte
+//    swizzle), plus a bulk copy of the item's query rows into the stream's Q
+//    buffer. Several streams per SM keep enough independent loads in flight
+//    to run HBM near its random-read ceiling.
+//  - FP8 pages land as 1-byte codes (+ E8M0 bytes for MXFP8); the consumer
+//    warp dequantises its stage to bf16 in shared memory (code * scale,
+//    rounded to bf16), so the HBM stream stays 1 byte per element.
+//  - The consumer warp owns all 16 query rows of its item (a GQA group of one
+//    or more queries sharing the node). Per stage it takes two pages (32
+//    tokens): q.k^T and p.v as m16n8k16 bf16 tensor-core tiles with f32
+//    accumulators, online softmax in the log2 domain, P split into two bf16
+//    terms so P.V keeps ~16 significant bits of P. At the end of the item it
+//    writes one normalised partial state per row straight from registers.
+// All waits are bounded mbarrier waits; a timeout sets an error word.
 // The arithmetic is ReferenceBackend::decode's
 // (crates/dendrite-core/src/attention/backend.rs:254-262) over the node's
 // tokens; partial states are merged by merge.cu along each query's path.
+#include <algorithm>
+
 #include "dd_device.cuh"
 
 namespace dd {
 
-constexpr int kMmaRows = 64;       // rows per item (4 warps x 16)
-constexpr int kMmaConsumers = 4;   // consumer warps
-constexpr int kMmaThreads = (kMmaConsumers + 1) * 32;
-constexpr int kStagePages = 4;
+constexpr int kMmaRows = 16;       // query rows per work item
+constexpr int kStreams = 4;        // consumer warps = independent streams
+constexpr int kMmaThreads = 2 * kStreams * 32;  // consumer warps, then producer warps
+constexpr int kStepPages = 2;      // pages per stage
+constexpr int kItemSlots = 2;      // item descriptors per stream
 
 enum KvKind { kKvBf16 = 0, kKvE4m3 = 1, kKvMx = 2 };
 
@@ -34,15 +45,15 @@ struct MmaCfg {
   static constexpr int kSliceBf16 = kPageSize * D * 2;                 // one page, K or V
   static constexpr int kSliceRaw = KV == kKvBf16 ? kSliceBf16 : kPageSize * D;
   static constexpr int kMxBytes = KV == kKvMx ? kPageSize * (D / 32) : 0;
-  static constexpr int kStages = KV == kKvBf16 ? (D == 128 ? 3 : 4) : 4;
-  static constexpr int kRawStage = 2 * kStagePages * kSliceRaw;        // K pages then V pages
-  static constexpr int kMxStage = 2 * kStagePages * kMxBytes;
-  static constexpr int kRawStageAll = kRawStage + (kMxStage ? ((kMxStage + 1023) / 1024) * 1024 : 0);
-  static constexpr int kConvBytes = KV == kKvBf16 ? 0 : 2 * kStagePages * kSliceBf16;
-  static constexpr int kCombineBytes = kMmaConsumers * 16 * D * 4 + 2 * kMmaConsumers * 16 * 4;
-  static constexpr int kPipeBytes = kStages * kRawStageAll + kConvBytes;
-  static constexpr int kSmemBytes =
-      (kPipeBytes > kCombineBytes ? kPipeBytes : kCombineBytes) + 1024;  // + alignment slack
+  static constexpr int kStages = 3;
+  static constexpr int kRawStage = 2 * kStepPages * kSliceRaw;         // K0 K1 V0 V1
+  static constexpr int kMxStage = 2 * kStepPages * kMxBytes;
+  static constexpr int kStageAll = kRawStage + (kMxStage ? ((kMxStage + 1023) / 1024) * 1024 : 0);
+  static constexpr int kConvBytes = KV == kKvBf16 ? 0 : 2 * kStepPages * kSliceBf16;
+  static constexpr int kQRowBytes = D * 2 + 16;                        // padded: conflict-free ldmatrix
+  static constexpr int kQBytes = ((kMmaRows * kQRowBytes + 1023) / 1024) * 1024;
+  static constexpr int kStreamBytes = kStages * kStageAll + kConvBytes + kQBytes;
+  static constexpr int kSmemBytes = kStreams * kStreamBytes + 1024;   // + alignment slack
 };
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
@@ -66,217 +77,387 @@ __device__ __forceinline__ void mma_bf16(float (&c)[4], const uint32_t (&a)[4], 
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+// 3-D TMA load (x, y, z) into shared memory with mbarrier completion.
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int32_t x, int32_t y,
+                                            int32_t z, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // Byte offset of 16-byte chunk `chunk` (8 bf16 along D) of token row `t`
-// inside a bf16 page slice stored as D/64 TMA boxes of [16][128 B] with the
+// inside a bf16 page slice stored as D/64 blocks of [16][128 B] with the
 // 128-byte swizzle (chunk index XOR row % 8).
 __device__ __forceinline__ uint32_t swz_bf16(int t, int chunk) {
   return (uint32_t)((chunk >> 3) * 2048 + t * 128 + (((chunk & 7) ^ (t & 7)) << 4));
 }
 
+struct StageMeta {
+  int8_t item_slot;
+  int8_t flags;    // 1 first stage of an item, 2 last stage, 4 no more work
+  int8_t np;       // pages in this stage (0..2)
+  int8_t invalid;  // bit j: page j has an out-of-range id (skipped)
+  int32_t page0;   // index of the stage's first page within the item
+};
+enum { kFirst = 1, kLast = 2, kDone = 4 };
+
+// Cycle accounting for pipeline experiments (off unless DD_EXPERIMENT_TIMING).
+#ifdef DD_EXPERIMENT_TIMING
+#define DD_TSTART(v) const long long v = clock64();
+#define DD_TACC(acc, v) acc += clock64() - v;
+#define DD_TFLUSH(a, slot, acc) \
+  atomicAdd(reinterpret_cast<unsigned long long*>(&(a).err->pad[1]) + (slot), (unsigned long long)(acc));
+#else
+#define DD_TSTART(v)
+#define DD_TACC(acc, v)
+#define DD_TFLUSH(a, slot, acc)
+#endif
+
+struct StreamShared {
+  uint64_t full[3];
+  uint64_t empty[3];
+  uint64_t q_empty;
+  StageMeta meta[3];
+  WorkItem items[kItemSlots];
+};
+
 template <int D, int KV>
-__global__ void __launch_bounds__(kMmaThreads)
+__global__ void __launch_bounds__(kMmaThreads, 1)
     attn_mma_kernel(const __grid_constant__ CUtensorMap kv_map, AttnArgs a) {
   using C = MmaCfg<D, KV>;
   constexpr int S = C::kStages;
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t full_bar[S];
-  __shared__ __align__(8) uint64_t empty_bar[S];
+  __shared__ StreamShared ss[kStreams];
   __shared__ int abort_flag;
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
-  uint8_t* conv = smem + S * C::kRawStageAll;
 
-  const uint32_t* pages;
-  const WorkItem it = resolve_item(a, pages, kMmaRows);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int npages = it.npages;
-  const int nst = (npages + kStagePages - 1) / kStagePages;
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < S; ++s) {
-      mbar_init(&full_bar[s], 1);
-      mbar_init(&empty_bar[s], kMmaConsumers);
+  if (threadIdx.x < kStreams) {
+    StreamShared& s = ss[threadIdx.x];
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&s.full[i], 1);
+      mbar_init(&s.empty[i], 1);
     }
+    mbar_init(&s.q_empty, 1);
+  }
+  if (threadIdx.x == 0) {
     abort_flag = 0;
     fence_mbar_init();
   }
-  if (threadIdx.x == kMmaConsumers * 32) prefetch_tmap(&kv_map);
+  if (threadIdx.x == kStreams * 32) prefetch_tmap(&kv_map);
   __syncthreads();
 
-  if (warp == kMmaConsumers) {
+  if (warp >= kStreams) {
     // ------------------------------------------------------------ producer
+    // Producer warp kStreams + c drives stream c from its lane 0, so a stall
+    // on one stream's reads never delays another stream.
+    const int c = warp - kStreams;
     if (lane == 0) {
-      for (int i = 0; i < nst; ++i) {
-        const int s = i % S;
-        if (i >= S && !mbar_wait(&empty_bar[s], ((i / S) - 1) & 1, &abort_flag, a.err)) break;
-        const int np = min(kStagePages, npages - i * kStagePages);
-        const uint32_t bytes = (uint32_t)np * 2 * (C::kSliceRaw + C::kMxBytes);
-        mbar_arrive_expect_tx(&full_bar[s], bytes);
-        uint8_t* st = smem + s * C::kRawStageAll;
-        for (int j = 0; j < np; ++j) {
-          uint32_t page = pages[i * kStagePages + j];
-          if (page >= (uint32_t)a.num_pages) {
-            report_error(a.err, kDevErrBadPage, page);
-            page = 0;  // load something harmless; consumers mask the page
+      StreamShared& sh = ss[c];
+      uint8_t* base = smem + c * C::kStreamBytes;
+      uint8_t* qbuf = base + S * C::kStageAll + C::kConvBytes;
+      int stage_idx = 0, item_count = 0;
+      bool need_item = true, finished = false;
+      WorkItem it{};
+      const uint32_t* pages = nullptr;
+      int pi = 0;                      // next page of the item
+      uint32_t nxt0 = 0, nxt1 = 0;     // prefetched ids of pages pi, pi+1
+      // The next item is prefetched one dependent read per stage (claim the
+      // index, read the item, read its first page ids), so the latency chain
+      // overlaps the current item's stages instead of stalling the stream.
+      int pf_state = 0, pf_idx = 0;
+      WorkItem pf_it{};
+      const uint32_t* pf_pages = nullptr;
+      uint32_t pf0 = 0, pf1 = 0;
+      auto pf_step = [&]() {
+        if (pf_state == 0) {
+          pf_idx = (int)atomicAdd(&a.err->work_counter, 1u);
+        } else if (pf_state == 1) {
+          if (pf_idx < a.num_items) pf_it = resolve_item_idx(a, pf_idx, pf_pages, kMmaRows);
+        } else if (pf_state == 2) {
+          if (pf_idx < a.num_items) {
+            pf0 = pf_it.npages > 0 ? pf_pages[0] : 0u;
+            pf1 = pf_it.npages > 1 ? pf_pages[1] : 0u;
           }
-          for (int kv = 0; kv < 2; ++kv) {
-            const int y = (int)((((int64_t)page * 2 + kv) * a.Hkv + it.kv_head) * kPageSize);
-            uint8_t* dst = st + (kv * kStagePages + j) * C::kSliceRaw;
-            if (KV == kKvBf16) {
+        }
+        ++pf_state;
+      };
+      long long t_pf = 0, t_empty = 0, t_qe = 0;
+      DD_TSTART(tlife)
+      uint64_t t_idle = global_ns();
+      while (!finished) {
+        if (abort_flag) break;
+        bool done = false;
+        if (need_item) {
+          DD_TSTART(tpf)
+          while (pf_state < 3) pf_step();  // completes the prefetch (or does it all when disabled)
+          DD_TACC(t_pf, tpf)
+          done = pf_idx >= a.num_items;
+          if (!done) {
+            it = pf_it;
+            pages = pf_pages;
+            pi = 0;
+            nxt0 = pf0;
+            nxt1 = pf1;
+          }
+          pf_state = 0;
+        }
+        // Wait (bounded, non-blocking poll) for a free stage.
+        const int s = stage_idx % S;
+        if (stage_idx >= S) {
+          DD_TSTART(tem)
+          while (!mbar_try_wait(&sh.empty[s], ((stage_idx / S) - 1) & 1)) {
+            if (global_ns() - t_idle > kWaitLimitNs) {
+              abort_flag = 1;
+              report_error(a.err, kDevErrWaitTimeout, 1);
+              break;
+            }
+          }
+          DD_TACC(t_empty, tem)
+          if (abort_flag) break;
+        }
+        // The Q buffer of the stream is reused once the consumer has read it.
+        DD_TSTART(tqe)
+        if (need_item && !done && item_count >= 1 &&
+            !mbar_wait(&sh.q_empty, (item_count - 1) & 1, &abort_flag, a.err))
+          break;
+        DD_TACC(t_qe, tqe)
+        StageMeta m;
+        uint32_t bytes = 0;
+        if (done) {
+          m.item_slot = 0;
+          m.flags = kDone;
+          m.np = 0;
+          m.invalid = 0;
+          m.page0 = 0;
+          finished = true;
+        } else {
+          const int k = item_count & 1;
+          if (need_item) sh.items[k] = it;
+          const int np = min(kStepPages, it.npages - pi);
+          uint32_t pg[2] = {nxt0, nxt1};
+          int invalid = 0;
+          for (int j = 0; j < np; ++j)
+            if (pg[j] >= (uint32_t)a.num_pages) {
+              report_error(a.err, kDevErrBadPage, pg[j]);
+              invalid |= 1 << j;
+              pg[j] = 0;  // load something harmless; the consumer skips the page
+            }
+          m.item_slot = (int8_t)k;
+          m.flags = (int8_t)((need_item ? kFirst : 0) | (pi + np >= it.npages ? kLast : 0));
+          m.np = (int8_t)np;
+          m.invalid = (int8_t)invalid;
+          m.page0 = pi;
+          sh.meta[s] = m;
+          const uint32_t qbytes = need_item ? (uint32_t)it.nrows * D * 2 : 0u;
+          bytes = (uint32_t)np * 2 * (C::kSliceRaw + C::kMxBytes) + qbytes;
+          mbar_arrive_expect_tx(&sh.full[s], bytes);
+          if (qbytes) {
+            // Read every row's query index first (independent loads), then
+            // issue the row copies.
+            const uint16_t* qsrc[kMmaRows];
 #pragma unroll
-              for (int hb = 0; hb < D / 64; ++hb)
-                tma_load_2d(dst + hb * 2048, &kv_map, hb * 64, y, &full_bar[s]);
-            } else {
-              tma_load_2d(dst, &kv_map, 0, y, &full_bar[s]);
-              if (KV == kKvMx) {
-                const uint8_t* src = reinterpret_cast<const uint8_t*>(a.scales) +
-                                     (size_t)y * (D / 32);
-                bulk_load(st + C::kRawStage + (kv * kStagePages + j) * C::kMxBytes, src,
-                          C::kMxBytes, &full_bar[s]);
+            for (int r = 0; r < kMmaRows; ++r) {
+              qsrc[r] = nullptr;
+              if (r < it.nrows) {
+                const int rr = it.row0 + r, qi = rr / a.g;
+                const int hq = qo_head_of(a.gqa_map, it.kv_head, rr % a.g, a.Hkv, a.g);
+                const int qid = a.qorder ? a.qorder[it.q_begin + qi] : it.q_begin + qi;
+                qsrc[r] = reinterpret_cast<const uint16_t*>(a.q) + ((size_t)qid * a.Hq + hq) * D;
               }
             }
+#pragma unroll
+            for (int r = 0; r < kMmaRows; ++r)
+              if (r < it.nrows) bulk_load(qbuf + r * C::kQRowBytes, qsrc[r], D * 2, &sh.full[s]);
+          }
+          uint8_t* st = base + s * C::kStageAll;
+          for (int j = 0; j < np; ++j)
+            for (int kv = 0; kv < 2; ++kv) {
+              const int y = (int)((((int64_t)pg[j] * 2 + kv) * a.Hkv + it.kv_head) * kPageSize);
+              uint8_t* dst = st + (kv * kStepPages + j) * C::kSliceRaw;
+              if (KV == kKvBf16 && D == 128)
+                tma_load_3d(dst, &kv_map, 0, y, 0, &sh.full[s]);
+              else
+                tma_load_2d(dst, &kv_map, 0, y, &sh.full[s]);
+              if (KV == kKvMx)
+                bulk_load(st + C::kRawStage + (kv * kStepPages + j) * C::kMxBytes,
+                          reinterpret_cast<const uint8_t*>(a.scales) + (size_t)y * (D / 32),
+                          C::kMxBytes, &sh.full[s]);
+            }
+          pi += np;
+          // Prefetch the next stage's page ids now; they are needed only after
+          // the next free-stage wait.
+          nxt0 = pi < it.npages ? pages[pi] : 0u;
+          nxt1 = pi + 1 < it.npages ? pages[pi + 1] : 0u;
+          if (need_item) need_item = false;
+          if (pi >= it.npages) {
+            need_item = true;
+            ++item_count;
           }
         }
-      }
-    }
-    // fall through to the final CTA barrier
-  } else {
-    // ------------------------------------------------------------ consumers
-    const int nrows = it.nrows;
-    int RG = (nrows + 15) / 16;
-    if (RG == 3) RG = 4;
-    const int TG = kMmaConsumers / RG;
-    const int rg = warp / TG, tg = warp % TG;
-    const int ctid = threadIdx.x;  // 0..127
-
-    // Query fragments (A operand, rows rg*16 + lane/4 and +8).
-    uint32_t qa[D / 16][4];
-    {
-      const int r0 = rg * 16 + (lane >> 2);
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        const int r = r0 + half * 8;
-        const uint32_t* qrow = nullptr;
-        if (r < nrows) {
-          const int rr = it.row0 + r, qi = rr / a.g;
-          const int hq = qo_head_of(a.gqa_map, it.kv_head, rr % a.g, a.Hkv, a.g);
-          const int qid = a.qorder ? a.qorder[it.q_begin + qi] : it.q_begin + qi;
-          qrow = reinterpret_cast<const uint32_t*>(reinterpret_cast<const uint16_t*>(a.q) +
-                                                   ((size_t)qid * a.Hq + hq) * D);
+        if (done) {
+          sh.meta[s] = m;
+          mbar_arrive_expect_tx(&sh.full[s], 0);
         }
+        ++stage_idx;
+        t_idle = global_ns();
+#ifndef DD_EXPERIMENT_NO_PREFETCH
+        if (!finished && pf_state < 3) pf_step();
+#endif
+      }
+      long long t_life = 0;
+      DD_TACC(t_life, tlife)
+      DD_TFLUSH(a, 2, t_empty)
+      DD_TFLUSH(a, 3, t_life)
+      DD_TFLUSH(a, 4, t_qe)
+      DD_TFLUSH(a, 5, t_pf)
+      (void)t_pf; (void)t_empty; (void)t_qe; (void)t_life;
+    }
+  } else {
+    // ------------------------------------------------------------ consumer
+    StreamShared& sh = ss[warp];
+    uint8_t* base = smem + warp * C::kStreamBytes;
+    uint8_t* conv = base + S * C::kStageAll;
+    uint8_t* qbuf = conv + C::kConvBytes;
+    WorkItem it{};
+    uint32_t qa[D / 16][4];
+    float o[D / 8][4];
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+    float sc_k = 1.f, sc_v = 1.f;
+    int items_started = 0;
+    long long t_full = 0;
+    DD_TSTART(tclife)
+    const int tc = (lane & 3) * 2;
+
+    for (int stage_idx = 0;; ++stage_idx) {
+      const int s = stage_idx % S;
+      DD_TSTART(tfw)
+      if (!mbar_wait(&sh.full[s], (stage_idx / S) & 1, &abort_flag, a.err)) break;
+      DD_TACC(t_full, tfw)
+      const StageMeta m = sh.meta[s];
+      if (m.flags & kDone) break;
+      if (m.flags & kFirst) {
+        it = sh.items[m.item_slot];
+        const uint32_t qbase = smem_u32(qbuf);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const int c = kk * 8 + (lane & 3);  // u32 index of (kk*16 + (lane%4)*2)
-          qa[kk][half] = qrow ? qrow[c] : 0u;
-          qa[kk][2 + half] = qrow ? qrow[c + 4] : 0u;
-        }
-      }
-    }
-    float o[D / 8][4];
-#pragma unroll
-    for (int n = 0; n < D / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
-    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
-
-    float sc_k = 1.f, sc_v = 1.f;
-    if (KV == kKvE4m3) {
-      sc_k = reinterpret_cast<const float*>(a.scales)[it.kv_head];
-      sc_v = reinterpret_cast<const float*>(a.scales)[a.Hkv + it.kv_head];
-    }
-
-    for (int i = 0; i < nst; ++i) {
-      const int s = i % S;
-      const bool ok = mbar_wait(&full_bar[s], (i / S) & 1, &abort_flag, a.err);
-      const int np = min(kStagePages, npages - i * kStagePages);
-      const uint8_t* kbase;
-      const uint8_t* vbase;
-      const uint8_t* st = smem + s * C::kRawStageAll;
-      if (KV == kKvBf16) {
-        kbase = st;
-        vbase = st + kStagePages * C::kSliceRaw;
-      } else {
-        // Dequantise the stage into the bf16 buffer: wait until every
-        // consumer is done with the previous contents first.
-        named_bar_sync(1, kMmaConsumers * 32);
-        if (ok) {
-          for (int u = ctid; u < np * 2 * kPageSize * (D / 16); u += kMmaConsumers * 32) {
-            const int c = u % (D / 16);            // 16-code chunk along D
-            const int t = (u / (D / 16)) % kPageSize;
-            const int kv = (u / (D / 16 * kPageSize)) & 1;
-            const int j = u / (D / 16 * kPageSize * 2);
-            const uint8_t* src = st + (kv * kStagePages + j) * C::kSliceRaw + t * D +
-                                 (((c & 7) ^ (t & 7)) << 4);
-            const uint4 codes = *reinterpret_cast<const uint4*>(src);
-            float sc;
-            if (KV == kKvE4m3) {
-              sc = kv ? sc_v : sc_k;
-            } else {
-              sc = e8m0_to_float(st[C::kRawStage + (kv * kStagePages + j) * C::kMxBytes +
-                                    t * (D / 32) + (c >> 1)]);
-            }
-            const uint32_t w[4] = {codes.x, codes.y, codes.z, codes.w};
-            uint32_t outw[8];
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              const float2 f0 = e4m3x2_to_float2((uint16_t)(w[q] & 0xffff));
-              const float2 f1 = e4m3x2_to_float2((uint16_t)(w[q] >> 16));
-              outw[2 * q] = pack_bf16x2(f0.x * sc, f0.y * sc);
-              outw[2 * q + 1] = pack_bf16x2(f1.x * sc, f1.y * sc);
-            }
-            uint8_t* dst = conv + (kv * kStagePages + j) * C::kSliceBf16;
-            *reinterpret_cast<uint4*>(dst + swz_bf16(t, 2 * c)) =
-                make_uint4(outw[0], outw[1], outw[2], outw[3]);
-            *reinterpret_cast<uint4*>(dst + swz_bf16(t, 2 * c + 1)) =
-                make_uint4(outw[4], outw[5], outw[6], outw[7]);
-          }
+          const int row = (lane & 7) + (((lane >> 3) & 1) << 3);
+          const int chunk = kk * 2 + (lane >> 4);
+          ldsm_x4(qbase + row * C::kQRowBytes + chunk * 16, qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3]);
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&empty_bar[s]);  // raw stage may be refilled
-        named_bar_sync(1, kMmaConsumers * 32);
-        kbase = conv;
-        vbase = conv + kStagePages * C::kSliceBf16;
+        if (lane == 0) mbar_arrive(&sh.q_empty);
+        ++items_started;
+#pragma unroll
+        for (int n = 0; n < D / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+        m0 = m1 = -INFINITY;
+        l0 = l1 = 0.f;
+        if (KV == kKvE4m3) {
+          sc_k = reinterpret_cast<const float*>(a.scales)[it.kv_head];
+          sc_v = reinterpret_cast<const float*>(a.scales)[a.Hkv + it.kv_head];
+        }
       }
-      if (ok) {
-        for (int jj = tg; jj < np; jj += TG) {
-          const int pi = i * kStagePages + jj;
-          int valid = (pi == npages - 1) ? it.last_valid : kPageSize;
-          if (pages[pi] >= (uint32_t)a.num_pages) valid = 0;
-          if (valid == 0) continue;
-          const uint32_t kaddr = smem_u32(kbase + jj * C::kSliceBf16);
-          const uint32_t vaddr = smem_u32(vbase + jj * C::kSliceBf16);
-          // S = Q K^T for 16 rows x 16 tokens.
-          float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const int t = ((lane >> 4) << 3) + (lane & 7);
-            const int chunk = kk * 2 + ((lane >> 3) & 1);
-            uint32_t b0, b1, b2, b3;
-            ldsm_x4(kaddr + swz_bf16(t, chunk), b0, b1, b2, b3);
-            mma_bf16(s0, qa[kk], b0, b1);
-            mma_bf16(s1, qa[kk], b2, b3);
+      const int np = m.np;
+      const uint8_t* st = base + s * C::kStageAll;
+      const uint8_t* kb;
+      const uint8_t* vb;
+      if (KV == kKvBf16) {
+        kb = st;
+        vb = st + kStepPages * C::kSliceRaw;
+      } else {
+        // Dequantise the stage's codes into the warp's bf16 buffer.
+        for (int u = lane; u < np * 2 * kPageSize * (D / 16); u += 32) {
+          const int c = u % (D / 16);            // 16-code chunk along D
+          const int t = (u / (D / 16)) % kPageSize;
+          const int j = (u / (D / 16 * kPageSize)) % np;
+          const int kv = u / (D / 16 * kPageSize * np);
+          const uint8_t* src = st + (kv * kStepPages + j) * C::kSliceRaw + t * D +
+                               (((c & 7) ^ (t & 7)) << 4);
+          const uint4 codes = *reinterpret_cast<const uint4*>(src);
+          float scl;
+          if (KV == kKvE4m3) {
+            scl = kv ? sc_v : sc_k;
+          } else {
+            scl = e8m0_to_float(st[C::kRawStage + (kv * kStepPages + j) * C::kMxBytes +
+                                   t * (D / 32) + (c >> 1)]);
           }
-          // Scale, mask, online softmax (log2 domain).
-          const int tc = (lane & 3) * 2;
-          float x[8] = {s0[0], s0[1], s1[0], s1[1], s0[2], s0[3], s1[2], s1[3]};
-          const int tok[4] = {tc, tc + 1, 8 + tc, 9 + tc};
+          const uint32_t w[4] = {codes.x, codes.y, codes.z, codes.w};
+          uint32_t outw[8];
 #pragma unroll
-          for (int e = 0; e < 8; ++e)
-            x[e] = tok[e & 3] < valid ? x[e] * a.scale_log2 : -INFINITY;
-          float mx0 = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3]));
-          float mx1 = fmaxf(fmaxf(x[4], x[5]), fmaxf(x[6], x[7]));
-          mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
-          mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
-          mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
-          mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-          const float nm0 = fmaxf(m0, mx0), nm1 = fmaxf(m1, mx1);
+          for (int q = 0; q < 4; ++q) {
+            const float2 f0 = e4m3x2_to_float2((uint16_t)(w[q] & 0xffff));
+            const float2 f1 = e4m3x2_to_float2((uint16_t)(w[q] >> 16));
+            outw[2 * q] = pack_bf16x2(f0.x * scl, f0.y * scl);
+            outw[2 * q + 1] = pack_bf16x2(f1.x * scl, f1.y * scl);
+          }
+          uint8_t* dst = conv + (kv * kStepPages + j) * C::kSliceBf16;
+          *reinterpret_cast<uint4*>(dst + swz_bf16(t, 2 * c)) =
+              make_uint4(outw[0], outw[1], outw[2], outw[3]);
+          *reinterpret_cast<uint4*>(dst + swz_bf16(t, 2 * c + 1)) =
+              make_uint4(outw[4], outw[5], outw[6], outw[7]);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sh.empty[s]);  // raw stage may be refilled
+        kb = conv;
+        vb = conv + kStepPages * C::kSliceBf16;
+      }
+      // Valid tokens per page of the step (0 = absent or skipped).
+      int valid[2];
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        valid[j] = j < np ? ((m.page0 + j == it.npages - 1) ? it.last_valid : kPageSize) : 0;
+        if ((m.invalid >> j) & 1) valid[j] = 0;
+#ifdef DD_EXPERIMENT_NO_COMPUTE
+        valid[j] = 0;  // data-movement ceiling experiment only
+#endif
+      }
+      if (valid[0] + valid[1] > 0) {
+        // S = Q K^T for 16 rows x 32 tokens: four independent n-tile chains.
+        float sacc[4][4];
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt) sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.f;
+        const uint32_t k0 = smem_u32(kb), k1 = smem_u32(kb + C::kSliceBf16);
+        const bool two = valid[1] > 0;
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const int t = ((lane >> 4) << 3) + (lane & 7);
+          const int chunk = kk * 2 + ((lane >> 3) & 1);
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4(k0 + swz_bf16(t, chunk), b0, b1, b2, b3);
+          mma_bf16(sacc[0], qa[kk], b0, b1);
+          mma_bf16(sacc[1], qa[kk], b2, b3);
+          if (two) {
+            ldsm_x4(k1 + swz_bf16(t, chunk), b0, b1, b2, b3);
+            mma_bf16(sacc[2], qa[kk], b0, b1);
+            mma_bf16(sacc[3], qa[kk], b2, b3);
+          }
+        }
+        // x[nt][0..1]: row lane/4, tokens nt*8+tc+{0,1}; x[nt][2..3]: row +8.
+        float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt) {
+          const int vj = valid[nt >> 1];
+          const int tok = (nt & 1) * 8 + tc;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const bool ok = tok + (c & 1) < vj;
+            sacc[nt][c] = ok ? sacc[nt][c] * a.scale_log2 : -INFINITY;
+          }
+          mx0 = fmaxf(mx0, fmaxf(sacc[nt][0], sacc[nt][1]));
+          mx1 = fmaxf(mx1, fmaxf(sacc[nt][2], sacc[nt][3]));
+        }
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+        const float nm0 = fmaxf(m0, mx0), nm1 = fmaxf(m1, mx1);
+        // Rescale the running state only when some row's max moved.
+        if (__any_sync(0xffffffffu, nm0 != m0 || nm1 != m1)) {
           const float al0 = fast_exp2(m0 - nm0), al1 = fast_exp2(m1 - nm1);
-          m0 = nm0;
-          m1 = nm1;
-          float p[8];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) p[e] = fast_exp2(x[e] - nm0);
-#pragma unroll
-          for (int e = 4; e < 8; ++e) p[e] = fast_exp2(x[e] - nm1);
-          l0 = l0 * al0 + (p[0] + p[1] + p[2] + p[3]);
-          l1 = l1 * al1 + (p[4] + p[5] + p[6] + p[7]);
+          l0 *= al0;
+          l1 *= al1;
 #pragma unroll
           for (int n = 0; n < D / 8; ++n) {
             o[n][0] *= al0;
@@ -284,14 +465,29 @@ __global__ void __launch_bounds__(kMmaThreads)
             o[n][2] *= al1;
             o[n][3] *= al1;
           }
-          // P = P_hi + P_lo, both bf16: the two P.V products carry P to
-          // ~16 significant bits, so rounding P costs no accuracy.
+          m0 = nm0;
+          m1 = nm1;
+        }
+        float p[4][4];
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt) {
+          p[nt][0] = fast_exp2(sacc[nt][0] - m0);
+          p[nt][1] = fast_exp2(sacc[nt][1] - m0);
+          p[nt][2] = fast_exp2(sacc[nt][2] - m1);
+          p[nt][3] = fast_exp2(sacc[nt][3] - m1);
+          l0 += p[nt][0] + p[nt][1];
+          l1 += p[nt][2] + p[nt][3];
+        }
+        // O += P V, one 16-token k-step per page; P = P_hi + P_lo (bf16).
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          if (j == 1 && !two) break;
           uint32_t pa[4], pl[4];
-          split_bf16x2(p[0], p[1], pa[0], pl[0]);
-          split_bf16x2(p[4], p[5], pa[1], pl[1]);
-          split_bf16x2(p[2], p[3], pa[2], pl[2]);
-          split_bf16x2(p[6], p[7], pa[3], pl[3]);
-          // O += P V.
+          split_bf16x2(p[2 * j][0], p[2 * j][1], pa[0], pl[0]);
+          split_bf16x2(p[2 * j][2], p[2 * j][3], pa[1], pl[1]);
+          split_bf16x2(p[2 * j + 1][0], p[2 * j + 1][1], pa[2], pl[2]);
+          split_bf16x2(p[2 * j + 1][2], p[2 * j + 1][3], pa[3], pl[3]);
+          const uint32_t vaddr = smem_u32(vb + j * C::kSliceBf16);
 #pragma unroll
           for (int nn = 0; nn < D / 16; ++nn) {
             const int t = (((lane >> 3) & 1) << 3) + (lane & 7);
@@ -307,58 +503,40 @@ __global__ void __launch_bounds__(kMmaThreads)
       }
       if (KV == kKvBf16) {
         __syncwarp();
-        if (lane == 0) mbar_arrive(&empty_bar[s]);
+        if (lane == 0) mbar_arrive(&sh.empty[s]);
       }
-    }
-
-    // Row sums across the quad.
-    l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
-    l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
-    l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
-    l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
-
-    // Stage every warp's state in shared memory (reusing the pipeline
-    // buffers), then combine the page-split warps and write partial states.
-    named_bar_sync(1, kMmaConsumers * 32);
-    float* cmb_o = reinterpret_cast<float*>(smem);                     // [warp][16][D]
-    float* cmb_m = cmb_o + kMmaConsumers * 16 * D;                     // [warp][16]
-    float* cmb_l = cmb_m + kMmaConsumers * 16;
-    {
-      float* wo = cmb_o + warp * 16 * D;
-      const int r = lane >> 2, c = (lane & 3) * 2;
+      if (m.flags & kLast) {
+        // Normalised partial state per row, written from registers.
+        float L0 = l0 + __shfl_xor_sync(0xffffffffu, l0, 1);
+        L0 += __shfl_xor_sync(0xffffffffu, L0, 2);
+        float L1 = l1 + __shfl_xor_sync(0xffffffffu, l1, 1);
+        L1 += __shfl_xor_sync(0xffffffffu, L1, 2);
 #pragma unroll
-      for (int n = 0; n < D / 8; ++n) {
-        *reinterpret_cast<float2*>(wo + r * D + n * 8 + c) = make_float2(o[n][0], o[n][1]);
-        *reinterpret_cast<float2*>(wo + (r + 8) * D + n * 8 + c) = make_float2(o[n][2], o[n][3]);
-      }
-      if ((lane & 3) == 0) {
-        cmb_m[warp * 16 + r] = m0;
-        cmb_m[warp * 16 + r + 8] = m1;
-        cmb_l[warp * 16 + r] = l0;
-        cmb_l[warp * 16 + r + 8] = l1;
-      }
-    }
-    named_bar_sync(1, kMmaConsumers * 32);
-    for (int idx = ctid; idx < nrows * D; idx += kMmaConsumers * 32) {
-      const int r = idx / D, d = idx % D;
-      const int rgr = r >> 4, rl = r & 15;
-      float M = -INFINITY;
-      for (int t = 0; t < TG; ++t) M = fmaxf(M, cmb_m[(rgr * TG + t) * 16 + rl]);
-      float L = 0.f, O = 0.f;
-      if (M != -INFINITY) {
-        for (int t = 0; t < TG; ++t) {
-          const int w = rgr * TG + t;
-          const float f = fast_exp2(cmb_m[w * 16 + rl] - M);
-          L += cmb_l[w * 16 + rl] * f;
-          O += cmb_o[(w * 16 + rl) * D + d] * f;
+        for (int half = 0; half < 2; ++half) {
+          const int r = (lane >> 2) + half * 8;
+          if (r >= it.nrows) continue;
+          const float L = half ? L1 : L0, M = half ? m1 : m0;
+          const float inv = L > 0.f ? 1.f / L : 0.f;
+          const int rr = it.row0 + r, qi = rr / a.g;
+          const int hq = qo_head_of(a.gqa_map, it.kv_head, rr % a.g, a.Hkv, a.g);
+          const int64_t slot = (int64_t)it.slot_base + (int64_t)qi * a.Hq + hq;
+          float* dst = a.part_o + slot * D + tc;
+#pragma unroll
+          for (int n = 0; n < D / 8; ++n)
+            *reinterpret_cast<float2*>(dst + n * 8) =
+                make_float2(o[n][2 * half] * inv, o[n][2 * half + 1] * inv);
+          if ((lane & 3) == 0) a.part_lse[slot] = L > 0.f ? M + log2f(L) : -INFINITY;
         }
       }
-      const int rr = it.row0 + r, qi = rr / a.g;
-      const int hq = qo_head_of(a.gqa_map, it.kv_head, rr % a.g, a.Hkv, a.g);
-      const int64_t slot = (int64_t)it.slot_base + (int64_t)qi * a.Hq + hq;
-      a.part_o[slot * D + d] = L > 0.f ? O / L : 0.f;
-      if (d == 0) a.part_lse[slot] = L > 0.f ? M + log2f(L) : -INFINITY;
     }
+    long long t_clife = 0;
+    DD_TACC(t_clife, tclife)
+    if (lane == 0) {
+      DD_TFLUSH(a, 0, t_full)
+      DD_TFLUSH(a, 1, t_clife)
+      DD_TFLUSH(a, 6, items_started)
+    }
+    (void)t_full; (void)t_clife;
   }
   __syncthreads();
 }
@@ -384,36 +562,56 @@ static PFN_encodeTiled get_encode_fn() {
   return fn;
 }
 
-// 2-D view of the page pool: rows = num_pages * 2 * Hkv * 16 token rows of
-// D elements; box = 16 rows x 128 bytes, 128-byte swizzle.
+// View of the page pool as rows = num_pages * 2 * Hkv * 16 token rows of D
+// elements with 128-byte swizzle. two_halves = 0: 2-D, box 16 rows x 128
+// bytes. two_halves = 1 (bf16, D = 128): 3-D (64 dims, rows, 2 halves of a
+// row) so one box of {64, 16, 2} moves a whole 4 KiB page slice, landing as
+// [half][16 rows][128 B].
 int make_kv_tensor_map(CUtensorMap* map, const void* kv, int64_t num_pages, int Hkv, int D,
-                       int elem_bytes) {
+                       int elem_bytes, int two_halves) {
   PFN_encodeTiled enc = get_encode_fn();
   if (!enc) return fail(DD_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   const uint64_t rows = (uint64_t)num_pages * 2 * Hkv * kPageSize;
   if (rows == 0 || rows > 0x7FFFFFFFull)  // y coordinates are int32
     return fail(DD_ERR_INVALID_ARGUMENT, "page pool too large for a TMA descriptor");
   if (((uintptr_t)kv & 15) != 0) return fail(DD_ERR_INVALID_ARGUMENT, "kv_pages not 16-byte aligned");
-  cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)D * elem_bytes};
-  cuuint32_t box[2] = {(cuuint32_t)(128 / elem_bytes), (cuuint32_t)kPageSize};
-  cuuint32_t estr[2] = {1, 1};
   const CUtensorMapDataType dt =
       elem_bytes == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
-  CUresult r = enc(map, dt, 2, const_cast<void*>(kv), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r;
+  if (two_halves) {
+    cuuint64_t dims[3] = {64, (cuuint64_t)rows, 2};
+    cuuint64_t strides[2] = {(cuuint64_t)D * elem_bytes, 128};
+    cuuint32_t box[3] = {64, (cuuint32_t)kPageSize, 2};
+    cuuint32_t estr[3] = {1, 1, 1};
+    r = enc(map, dt, 3, const_cast<void*>(kv), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  } else {
+    cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)D * elem_bytes};
+    cuuint32_t box[2] = {(cuuint32_t)(128 / elem_bytes), (cuuint32_t)kPageSize};
+    cuuint32_t estr[2] = {1, 1};
+    r = enc(map, dt, 2, const_cast<void*>(kv), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  }
   if (r != CUDA_SUCCESS) return fail(DD_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
   return DD_OK;
 }
 
 template <int D, int KV>
-static cudaError_t launch_mma_t(const CUtensorMap& map, const AttnArgs& a, dim3 grid,
-                                cudaStream_t st) {
+static cudaError_t launch_mma_t(const CUtensorMap& map, const AttnArgs& a, cudaStream_t st) {
   const int smem = MmaCfg<D, KV>::kSmemBytes;
   cudaError_t e = cudaFuncSetAttribute(attn_mma_kernel<D, KV>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
+  int dev = 0, sms = 148, per_sm = 1;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, attn_mma_kernel<D, KV>, kMmaThreads, smem);
+  if (e != cudaSuccess) return e;
+  const int ctas_needed = (a.num_items + kStreams - 1) / kStreams;
+  const int grid = std::max(1, std::min(ctas_needed, sms * std::max(per_sm, 1)));
   {
     ProfScope ps(kProfMma, st);
     attn_mma_kernel<D, KV><<<grid, kMmaThreads, smem, st>>>(map, a);
@@ -427,19 +625,24 @@ bool mma_supported(int D, int kv_dtype) {
   return false;
 }
 
-int launch_attn_mma(const AttnArgs& a, int64_t num_pages, dim3 grid, cudaStream_t st) {
+int mma_row_tile() { return kMmaRows; }
+
+// Launches the persistent kernel over a.num_items work items. The work
+// counter in the workspace header must be zero (the caller resets the header).
+int launch_attn_mma(const AttnArgs& a, int64_t num_pages, cudaStream_t st) {
+  if (a.num_items <= 0) return DD_OK;
   CUtensorMap map;
   const int eb = a.kv_dtype == DD_DTYPE_BF16 ? 2 : 1;
-  int rc = make_kv_tensor_map(&map, a.kv, num_pages, a.Hkv, a.D, eb);
+  int rc = make_kv_tensor_map(&map, a.kv, num_pages, a.Hkv, a.D, eb,
+                              a.kv_dtype == DD_DTYPE_BF16 && a.D == 128);
   if (rc) return rc;
   cudaError_t e;
   if (a.kv_dtype == DD_DTYPE_BF16)
-    e = a.D == 64 ? launch_mma_t<64, kKvBf16>(map, a, grid, st)
-                  : launch_mma_t<128, kKvBf16>(map, a, grid, st);
+    e = a.D == 64 ? launch_mma_t<64, kKvBf16>(map, a, st) : launch_mma_t<128, kKvBf16>(map, a, st);
   else if (a.kv_dtype == DD_DTYPE_E4M3)
-    e = launch_mma_t<128, kKvE4m3>(map, a, grid, st);
+    e = launch_mma_t<128, kKvE4m3>(map, a, st);
   else
-    e = launch_mma_t<128, kKvMx>(map, a, grid, st);
+    e = launch_mma_t<128, kKvMx>(map, a, st);
   if (e != cudaSuccess) return fail(DD_ERR_CUDA, std::string("attn_mma launch: ") + cudaGetErrorString(e));
   return DD_OK;
 }

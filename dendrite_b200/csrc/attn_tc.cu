@@ -279,12 +279,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           for (int i = 0; i < 32; ++i) s[c * 32 + i] = t[i];
         }
       }
-      float mt = -INFINITY;
+      // Max on the raw scores (the scale is positive), masked only on the
+      // partial last tile.
+      if (valid < kTcTok) {
 #pragma unroll
-      for (int i = 0; i < 128; ++i) {
-        s[i] = (i < valid) ? s[i] * a.scale_log2 : -INFINITY;
-        mt = fmaxf(mt, s[i]);
+        for (int i = 0; i < 128; ++i)
+          if (i >= valid) s[i] = -INFINITY;
       }
+      float mr0 = s[0], mr1 = s[1];
+#pragma unroll
+      for (int i = 2; i < 128; i += 2) {
+        mr0 = fmaxf(mr0, s[i]);
+        mr1 = fmaxf(mr1, s[i + 1]);
+      }
+      float mt = fmaxf(mr0, mr1) * a.scale_log2;
       if (!ok) mt = m_used;
       // Warp-uniform decision (tcgen05.ld/st are warp-collective).
       if (__any_sync(0xffffffffu, mt > m_used + kRescaleThreshold)) {
@@ -306,13 +314,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         l *= f;
         m_used = m_new;
       }
-      float sum = 0.f;
+      float sum0 = 0.f, sum1 = 0.f;
+      const float neg_m = -m_used;
 #pragma unroll
-      for (int i = 0; i < 128; ++i) {
-        s[i] = fast_exp2(s[i] - m_used);  // masked tokens: exp2(-inf) = 0
-        sum += s[i];
+      for (int i = 0; i < 128; i += 2) {
+        s[i] = fast_exp2(fmaf(s[i], a.scale_log2, neg_m));  // masked: exp2(-inf) = 0
+        s[i + 1] = fast_exp2(fmaf(s[i + 1], a.scale_log2, neg_m));
+        sum0 += s[i];
+        sum1 += s[i + 1];
       }
-      l += sum;
+      l += sum0 + sum1;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t hi[16], lo[16];
@@ -367,13 +378,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 }
 
 int make_kv_tensor_map(CUtensorMap* map, const void* kv, int64_t num_pages, int Hkv, int D,
-                       int elem_bytes);
+                       int elem_bytes, int two_halves);
 
 int launch_attn_tc(const AttnArgs& a, int64_t num_pages, int num_items, cudaStream_t st) {
   if (a.D != 128 || a.kv_dtype != DD_DTYPE_BF16 || a.q_dtype != DD_DTYPE_BF16)
     return fail(DD_ERR_NOT_AVAILABLE, "tcgen05 path: bf16 KV and queries, head_dim 128");
   CUtensorMap map;
-  int rc = make_kv_tensor_map(&map, a.kv, num_pages, a.Hkv, a.D, 2);
+  int rc = make_kv_tensor_map(&map, a.kv, num_pages, a.Hkv, a.D, 2, 0);
   if (rc) return rc;
   cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        kTcSmem);

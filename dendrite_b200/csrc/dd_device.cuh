@@ -22,8 +22,9 @@ enum DeviceError : uint32_t {
 };
 struct WsHeader {
   uint32_t error;      // first error code (DeviceError)
-  uint32_t error_aux;  // e.g. offending page id
-  uint32_t pad[62];
+  uint32_t error_aux;     // e.g. offending page id
+  uint32_t work_counter;  // next work item of a persistent kernel (zeroed per call)
+  uint32_t pad[61];
 };
 static_assert(sizeof(WsHeader) == kWsHeaderBytes, "workspace header");
 
@@ -66,14 +67,17 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
-// Two-term bf16 split of a pair: x = hi + lo with hi = bf16(x) and
-// lo = bf16(x - hi) (the subtraction is exact in f32).
+// Two-term bf16 split of a pair of non-negative finite floats (softmax
+// probabilities): x = hi + lo + e with hi = x truncated to bf16, lo = (x - hi)
+// truncated to bf16 (x - hi is exact in f32). |e| < 2^-14 |x|. Only integer
+// and f32 add units are used (no conversion instructions), so the split costs
+// nothing on the pipe that also evaluates the exponentials.
 __device__ __forceinline__ void split_bf16x2(float a, float b, uint32_t& hi, uint32_t& lo) {
-  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
-  const float2 hf = __bfloat1622float2(h);
-  __nv_bfloat162 l = __floats2bfloat162_rn(a - hf.x, b - hf.y);
-  hi = *reinterpret_cast<uint32_t*>(&h);
-  lo = *reinterpret_cast<uint32_t*>(&l);
+  const uint32_t ua = __float_as_uint(a), ub = __float_as_uint(b);
+  hi = __byte_perm(ua, ub, 0x7632);  // high halves: a in the low 16 bits
+  const float ra = a - __uint_as_float(ua & 0xffff0000u);
+  const float rb = b - __uint_as_float(ub & 0xffff0000u);
+  lo = __byte_perm(__float_as_uint(ra), __float_as_uint(rb), 0x7632);
 }
 
 // ------------------------------------------------------------------- timing
@@ -193,6 +197,7 @@ struct AttnArgs {
   const int32_t* page_indptr;
   const int32_t* num_tokens;
   int32_t batch, nsplit, row_tiles;
+  int32_t num_items;       // work items of this launch (persistent kernels)
   // config
   int32_t Hq, Hkv, g, D, kv_dtype, q_dtype, gqa_map, num_pages;
   float scale_log2;        // softmax scale * log2(e)
@@ -210,6 +215,35 @@ __device__ __forceinline__ WorkItem resolve_item(const AttnArgs& a, const uint32
   }
   const int s = blockIdx.x, b = blockIdx.z;
   const int h = blockIdx.y / a.row_tiles, t = blockIdx.y % a.row_tiles;
+  const int ntok = a.num_tokens[b];
+  const int P = (ntok + kPageSize - 1) / kPageSize;
+  const int pb = (int)((int64_t)s * P / a.nsplit), pe = (int)((int64_t)(s + 1) * P / a.nsplit);
+  it.page_off = 0;
+  it.npages = pe - pb;
+  it.last_valid = (pe == P && (ntok % kPageSize)) ? ntok % kPageSize : kPageSize;
+  it.kv_head = h;
+  it.row0 = t * row_tile_rows;
+  it.nrows = min(row_tile_rows, a.g - it.row0);
+  it.q_begin = b;
+  it.slot_base = (s * a.batch + b) * a.Hq;
+  pages = a.pages + a.page_indptr[b] + pb;
+  return it;
+}
+
+// Same, for persistent kernels: work item `idx` of `a.num_items`. Flat mode
+// enumerates (split, KV head x row tile, query) with the split fastest.
+__device__ __forceinline__ WorkItem resolve_item_idx(const AttnArgs& a, int idx,
+                                                     const uint32_t*& pages, int row_tile_rows) {
+  WorkItem it;
+  if (a.items) {
+    it = a.items[idx];
+    pages = a.pages + it.page_off;
+    return it;
+  }
+  const int s = idx % a.nsplit;
+  const int rest = idx / a.nsplit;
+  const int y = rest % (a.Hkv * a.row_tiles), b = rest / (a.Hkv * a.row_tiles);
+  const int h = y / a.row_tiles, t = y % a.row_tiles;
   const int ntok = a.num_tokens[b];
   const int P = (ntok + kPageSize - 1) / kPageSize;
   const int pb = (int)((int64_t)s * P / a.nsplit), pe = (int)((int64_t)(s + 1) * P / a.nsplit);
