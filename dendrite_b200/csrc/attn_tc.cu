@@ -114,6 +114,14 @@ __device__ __forceinline__ void tmem_st16u(uint32_t taddr, const uint32_t (&v)[1
       : "memory");
 }
 
+// Wait-time accounting for pipeline experiments (off unless DD_EXPERIMENT_TIMING).
+#ifdef DD_EXPERIMENT_TIMING
+#define TCW(slot, expr) ([&]() { const long long _t0 = clock64(); const bool _r = (expr); \
+                                 tacc[slot] += clock64() - _t0; return _r; }())
+#else
+#define TCW(slot, expr) (expr)
+#endif
+
 struct TcBars {
   uint64_t kv_full[kTcSlots];
   uint64_t kv_empty[kTcSlots];
@@ -138,6 +146,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int npages = it.npages;
   const int ntiles = (npages + 7) / 8;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  long long tacc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  (void)tacc;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kTcSlots; ++s) {
@@ -169,29 +179,39 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   if (warp == 0) {
     // -------------------------------------------------------------- producer
-    if (lane == 0) {
+    // The whole warp produces: lane pj < 8 owns page pj of every tile and
+    // reads its id one tile ahead, so no global read sits between the
+    // free-slot wait and the copies.
+    {
       const int64_t rows_total = (int64_t)a.num_pages * 2 * a.Hkv * kPageSize;
+      const int pj = lane & 7;
+      uint32_t cur = (lane < 8 && pj < npages) ? pages[pj] : 0xFFFFFFFFu;
+      uint32_t nxt = 0xFFFFFFFFu;
       for (int idx = 0; idx < 2 * ntiles; ++idx) {
         const int s = idx % kTcSlots;
-        if (idx >= kTcSlots &&
-            !mbar_wait(&bars.kv_empty[s], ((idx / kTcSlots) - 1) & 1, abort, a.err))
-          break;
         const int j = idx >> 1, kv = idx & 1;
-        mbar_arrive_expect_tx(&bars.kv_full[s], kTcSlotBytes);
-        uint8_t* dst = slots + s * kTcSlotBytes;
-        for (int pj = 0; pj < 8; ++pj) {
-          const int pi = j * 8 + pj;
-          int y = (int)rows_total;  // past the end: TMA fills zeros
-          if (pi < npages) {
-            const uint32_t page = pages[pi];
-            if (page < (uint32_t)a.num_pages)
-              y = (int)((((int64_t)page * 2 + kv) * a.Hkv + it.kv_head) * kPageSize);
+        if (kv == 0 && lane < 8) {
+          const int pn = (j + 1) * 8 + pj;
+          nxt = pn < npages ? pages[pn] : 0xFFFFFFFFu;
+        }
+        if (idx >= kTcSlots &&
+            !TCW(6, mbar_wait(&bars.kv_empty[s], ((idx / kTcSlots) - 1) & 1, abort, a.err)))
+          break;
+        if (lane == 0) mbar_arrive_expect_tx(&bars.kv_full[s], kTcSlotBytes);
+        __syncwarp();
+        if (lane < 8) {
+          uint8_t* dst = slots + s * kTcSlotBytes;
+          int y = (int)rows_total;  // absent page: past the end, TMA fills zeros
+          if (cur != 0xFFFFFFFFu) {
+            if (cur < (uint32_t)a.num_pages)
+              y = (int)((((int64_t)cur * 2 + kv) * a.Hkv + it.kv_head) * kPageSize);
             else
-              report_error(a.err, kDevErrBadPage, page);
+              report_error(a.err, kDevErrBadPage, cur);
           }
           tma_load_2d(dst + pj * 2048, &kv_map, 0, y, &bars.kv_full[s]);
           tma_load_2d(dst + 16384 + pj * 2048, &kv_map, 64, y, &bars.kv_full[s]);
         }
+        if (kv == 1) cur = nxt;
       }
     }
   } else if (warp == 1) {
@@ -204,8 +224,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       tc_fence_after();
       auto issue_qk = [&](int j) -> bool {
         const int s = (2 * j) % kTcSlots;
-        if (!mbar_wait(&bars.kv_full[s], ((2 * j) / kTcSlots) & 1, abort, a.err)) return false;
-        if (j >= 2 && !mbar_wait(&bars.o_done, (j - 2) & 1, abort, a.err)) return false;
+        if (!TCW(2, mbar_wait(&bars.kv_full[s], ((2 * j) / kTcSlots) & 1, abort, a.err))) return false;
+        if (j >= 2 && !TCW(3, mbar_wait(&bars.o_done, (j - 2) & 1, abort, a.err))) return false;
         tc_fence_after();
         const uint32_t d = tbase + (uint32_t)(j & 1) * 128;
         const uint32_t kb = slot_addr + s * kTcSlotBytes;
@@ -222,9 +242,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       if (ok) ok = issue_qk(0);
       for (int j = 0; ok && j < ntiles; ++j) {
         if (j + 1 < ntiles && !issue_qk(j + 1)) break;
-        if (!mbar_wait(&bars.p_full[j & 1], (j >> 1) & 1, abort, a.err)) break;
+        if (!TCW(4, mbar_wait(&bars.p_full[j & 1], (j >> 1) & 1, abort, a.err))) break;
         const int s = (2 * j + 1) % kTcSlots;
-        if (!mbar_wait(&bars.kv_full[s], ((2 * j + 1) / kTcSlots) & 1, abort, a.err)) break;
+        if (!TCW(5, mbar_wait(&bars.kv_full[s], ((2 * j + 1) / kTcSlots) & 1, abort, a.err))) break;
         tc_fence_after();
         const uint32_t vb = slot_addr + s * kTcSlotBytes;
         const uint32_t p_tmem = tbase + (uint32_t)(j & 1) * 128;
@@ -264,7 +284,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     float m_used = -INFINITY, l = 0.f;
     for (int j = 0; j < ntiles; ++j) {
-      bool ok = mbar_wait(&bars.s_full[j & 1], (j >> 1) & 1, abort, a.err);
+      bool ok = TCW(0, mbar_wait(&bars.s_full[j & 1], (j >> 1) & 1, abort, a.err));
       tc_fence_after();
       const int valid = (j == ntiles - 1) ? (npages - 8 * j - 1) * kPageSize + it.last_valid : kTcTok;
       const uint32_t sb = lane_base + (uint32_t)(j & 1) * 128;
@@ -299,7 +319,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const float m_new = fmaxf(m_used, mt);
         const float f = fast_exp2(m_used - m_new);  // 0 when m_used is -inf
         if (j > 0) {
-          if (!mbar_wait(&bars.o_done, (j - 1) & 1, abort, a.err)) ok = false;
+          if (!TCW(1, mbar_wait(&bars.o_done, (j - 1) & 1, abort, a.err))) ok = false;
           tc_fence_after();
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
@@ -368,6 +388,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     if (live) a.part_lse[slot] = l > 0.f ? m_used + log2f(l) : -INFINITY;
   }
+#ifdef DD_EXPERIMENT_TIMING
+  if (lane == 0)
+    for (int k = 0; k < 8; ++k)
+      if (tacc[k])
+        atomicAdd(reinterpret_cast<unsigned long long*>(&a.err->pad[1]) + 8 + k, (unsigned long long)tacc[k]);
+#endif
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
