@@ -5,19 +5,28 @@
 //
 // One CTA per work item = (node, KV head, 128-row tile, page range):
 //   warp 0      TMA producer: K and V tiles of 128 tokens (8 pages x 2 boxes
-//               of [16 tokens][64 dims], 128-byte swizzle) into a 4-slot ring;
-//   warp 1      allocates 384 TMEM columns; lane 0 issues every tcgen05.mma:
-//                 S_j = Q . K_j^T      (A = Q, B = K tile, both K-major smem)
-//                 O  += P_j . V_j      (A = P in TMEM, B = V tile MN-major)
-//               and signals completion with tcgen05.commit on mbarriers;
-//   warps 2-5   softmax: thread r owns query row r (= TMEM lane r), loads
-//               its S row, keeps the running max / sum in the log2 domain,
-//               writes P over the S columns as two bf16 terms (hi + lo, so
-//               the P.V product keeps ~16 significant bits of P), and
-//               rescales its O row in TMEM only when its max grows by more
-//               than 2^8 (otherwise exponentials use the stale max, exactly).
-// S is double-buffered in TMEM so Q.K_{j+1} runs while the softmax of tile j
-// does; P.V of tile j overlaps the softmax of tile j+1.
+//               of [16 tokens][64 dims], 128-byte swizzle) into a 5-slot
+//               ring; lane p owns page p of each tile and reads its id one
+//               tile ahead;
+//   warp 1      allocates all 512 TMEM columns; lane 0 issues every
+//               tcgen05.mma and signals completion with tcgen05.commit:
+//                 S_j = Q . K_j^T   (A = Q, B = K tile, both K-major smem;
+//                                   S double-buffered, so Q.K_{j+1} runs
+//                                   while the softmax of tile j does)
+//                 O  += P_j . V_j   (A = P in TMEM, B = V tile MN-major)
+//   warps 2-9   softmax: each query row r (= TMEM lane r) is shared by two
+//               threads of two warps, one per 64-column half of the tile.
+//               Per tile they exchange only their partial row max through
+//               shared memory, keep the running max in the log2 domain and
+//               a partial sum each, write P as two bf16 terms (hi + lo, so
+//               P.V keeps ~16 significant bits of P) into the P columns, and
+//               rescale their half of the O row only when the max grows by
+//               more than 2^8 (otherwise the exponentials use the stale max,
+//               which is exact).
+// TMEM columns: S0 0-127, S1 128-255, P 256-383 (hi 256-319, lo 320-383),
+// O 384-511. Each tcgen05.mma costs the single issuing thread a fixed time,
+// so tiles are 128 tokens (N = 128) to keep that below the tensor work and
+// to amortise the shared-memory reads of the A operand.
 //
 // The arithmetic is ReferenceBackend::decode's
 // (crates/dendrite-core/src/attention/backend.rs:254-262) over the node's
@@ -27,17 +36,20 @@
 
 namespace dd {
 
-constexpr int kTcRows = 128;
+constexpr int kTcRows = 128;            // rows per item
 constexpr int kTcTok = 128;             // tokens per tile
-constexpr int kTcSlots = 4;             // K/V ring slots (32 KiB each)
-constexpr int kTcThreads = 192;
-constexpr int kTcSlotBytes = kTcTok * 128 * 2;  // 128 tokens x 128 dims bf16
-constexpr int kTcQBytes = kTcRows * 128 * 2;
+constexpr int kTcPagesPerTile = kTcTok / kPageSize;
+constexpr int kTcSlots = 5;             // K/V ring slots (32 KiB each)
+constexpr int kTcThreads = 320;
+constexpr int kTcSlotBytes = kTcTok * 128 * 2;   // 128 tokens x 128 dims bf16
+constexpr int kTcHalfBytes = kTcTok * 128;       // one 64-dim half of a slot
+constexpr int kTcQBytes = 128 * 128 * 2;
 constexpr int kTcSmem = kTcQBytes + kTcSlots * kTcSlotBytes + 1024;
-constexpr uint32_t kTmemCols = 512;     // power of two >= 384 (S0, S1, O)
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColS = 0, kColP = 256, kColO = 384;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
-// Instruction descriptor, kind::f16: D f32, A/B bf16, M = 128, N = 128.
+// Instruction descriptors, kind::f16, D f32, A/B bf16, M = 128, N = 128.
 constexpr uint32_t kIdescQK = (1u << 4) | (1u << 7) | (1u << 10) | ((128u >> 3) << 17) |
                               ((128u >> 4) << 24);
 constexpr uint32_t kIdescPV = kIdescQK | (1u << 16);  // B (V) is MN-major
@@ -121,43 +133,58 @@ __device__ __forceinline__ void tmem_st16u(uint32_t taddr, const uint32_t (&v)[1
 #else
 #define TCW(slot, expr) (expr)
 #endif
+#ifdef DD_EXPERIMENT_TIMING
+#define TCP_START(v) long long v = clock64();
+#define TCP_MARK(slot, v) { const long long _n = clock64(); tacc2[slot] += _n - v; v = _n; }
+#else
+#define TCP_START(v)
+#define TCP_MARK(slot, v)
+#endif
+
 
 struct TcBars {
   uint64_t kv_full[kTcSlots];
   uint64_t kv_empty[kTcSlots];
   uint64_t s_full[2];
-  uint64_t p_full[2];
+  uint64_t p_full;
   uint64_t o_done;
   uint64_t q_ready;
   uint32_t tmem_base;
   int abort;
+  float xmax[2][2][128];  // [tile parity][column half][row]: partial row max
+  float xsum[2][128];     // [column half][row]: partial row sum (epilogue)
 };
+
+__device__ __forceinline__ void pair_sync(int quarter) {
+  named_bar_sync(1 + quarter, 64);  // the two warps that share TMEM lanes of `quarter`
+}
 
 __global__ void __launch_bounds__(kTcThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap kv_map, AttnArgs a) {
   extern __shared__ uint8_t smem_raw[];
   __shared__ TcBars bars;
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
-  uint8_t* q_s = smem;
-  uint8_t* slots = smem + kTcQBytes;
+  uint8_t* q_s = smem;                  // [2 dim-halves][128 rows][128 B]
+  uint8_t* slots = smem + kTcQBytes;    // [slot][2 dim-halves][128 rows][128 B]
 
   const WorkItem it = a.items[blockIdx.x];
   const uint32_t* pages = a.pages + it.page_off;
   const int npages = it.npages;
-  const int ntiles = (npages + 7) / 8;
+  const int ntiles = (npages + kTcPagesPerTile - 1) / kTcPagesPerTile;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   long long tacc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  long long tacc2[8] = {0, 0, 0, 0, 0, 0, 0, 0};
   (void)tacc;
+  (void)tacc2;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kTcSlots; ++s) {
       mbar_init(&bars.kv_full[s], 1);
       mbar_init(&bars.kv_empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(&bars.s_full[b], 1);
-      mbar_init(&bars.p_full[b], 128);
-    }
+    mbar_init(&bars.s_full[0], 1);
+    mbar_init(&bars.s_full[1], 1);
+    mbar_init(&bars.p_full, 256);
     mbar_init(&bars.o_done, 1);
     mbar_init(&bars.q_ready, 128);
     bars.abort = 0;
@@ -179,91 +206,103 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   if (warp == 0) {
     // -------------------------------------------------------------- producer
-    // The whole warp produces: lane pj < 8 owns page pj of every tile and
-    // reads its id one tile ahead, so no global read sits between the
-    // free-slot wait and the copies.
-    {
-      const int64_t rows_total = (int64_t)a.num_pages * 2 * a.Hkv * kPageSize;
-      const int pj = lane & 7;
-      uint32_t cur = (lane < 8 && pj < npages) ? pages[pj] : 0xFFFFFFFFu;
-      uint32_t nxt = 0xFFFFFFFFu;
-      for (int idx = 0; idx < 2 * ntiles; ++idx) {
-        const int s = idx % kTcSlots;
-        const int j = idx >> 1, kv = idx & 1;
-        if (kv == 0 && lane < 8) {
-          const int pn = (j + 1) * 8 + pj;
-          nxt = pn < npages ? pages[pn] : 0xFFFFFFFFu;
-        }
-        if (idx >= kTcSlots &&
-            !TCW(6, mbar_wait(&bars.kv_empty[s], ((idx / kTcSlots) - 1) & 1, abort, a.err)))
-          break;
-        if (lane == 0) mbar_arrive_expect_tx(&bars.kv_full[s], kTcSlotBytes);
-        __syncwarp();
-        if (lane < 8) {
-          uint8_t* dst = slots + s * kTcSlotBytes;
-          int y = (int)rows_total;  // absent page: past the end, TMA fills zeros
-          if (cur != 0xFFFFFFFFu) {
-            if (cur < (uint32_t)a.num_pages)
-              y = (int)((((int64_t)cur * 2 + kv) * a.Hkv + it.kv_head) * kPageSize);
-            else
-              report_error(a.err, kDevErrBadPage, cur);
-          }
-          tma_load_2d(dst + pj * 2048, &kv_map, 0, y, &bars.kv_full[s]);
-          tma_load_2d(dst + 16384 + pj * 2048, &kv_map, 64, y, &bars.kv_full[s]);
-        }
-        if (kv == 1) cur = nxt;
+    // Lane p < 8 owns page p of every tile and reads its id one tile ahead,
+    // so no global read sits between the free-slot wait and the copies.
+    const int64_t rows_total = (int64_t)a.num_pages * 2 * a.Hkv * kPageSize;
+    const int pj = lane & (kTcPagesPerTile - 1);
+    const bool mine = lane < kTcPagesPerTile;
+    uint32_t cur = (mine && pj < npages) ? pages[pj] : 0xFFFFFFFFu;
+    uint32_t nxt = 0xFFFFFFFFu;
+    for (int idx = 0; idx < 2 * ntiles; ++idx) {
+      const int s = idx % kTcSlots;
+      const int j = idx >> 1, kv = idx & 1;
+      if (kv == 0 && mine) {
+        const int pn = (j + 1) * kTcPagesPerTile + pj;
+        nxt = pn < npages ? pages[pn] : 0xFFFFFFFFu;
       }
+      if (idx >= kTcSlots &&
+          !TCW(6, mbar_wait(&bars.kv_empty[s], ((idx / kTcSlots) - 1) & 1, abort, a.err)))
+        break;
+      if (lane == 0) mbar_arrive_expect_tx(&bars.kv_full[s], kTcSlotBytes);
+      __syncwarp();
+      if (mine) {
+        uint8_t* dst = slots + s * kTcSlotBytes;
+        int y = (int)rows_total;  // absent page: past the end, TMA fills zeros
+        if (cur != 0xFFFFFFFFu) {
+          if (cur < (uint32_t)a.num_pages)
+            y = (int)((((int64_t)cur * 2 + kv) * a.Hkv + it.kv_head) * kPageSize);
+          else
+            report_error(a.err, kDevErrBadPage, cur);
+        }
+        tma_load_2d(dst + pj * 2048, &kv_map, 0, y, &bars.kv_full[s]);
+        tma_load_2d(dst + kTcHalfBytes + pj * 2048, &kv_map, 64, y, &bars.kv_full[s]);
+      }
+      if (kv == 1) cur = nxt;
     }
   } else if (warp == 1) {
     // --------------------------------------------------------- MMA issuer
     if (lane == 0 && ntiles > 0) {
       const uint32_t q_addr = smem_u32(q_s);
       const uint32_t slot_addr = smem_u32(slots);
-      const uint32_t o_tmem = tbase + 256;
-      bool ok = mbar_wait(&bars.q_ready, 0, abort, a.err);
-      tc_fence_after();
-      auto issue_qk = [&](int j) -> bool {
-        const int s = (2 * j) % kTcSlots;
-        if (!TCW(2, mbar_wait(&bars.kv_full[s], ((2 * j) / kTcSlots) & 1, abort, a.err))) return false;
-        if (j >= 2 && !TCW(3, mbar_wait(&bars.o_done, (j - 2) & 1, abort, a.err))) return false;
-        tc_fence_after();
-        const uint32_t d = tbase + (uint32_t)(j & 1) * 128;
-        const uint32_t kb = slot_addr + s * kTcSlotBytes;
+      // Descriptors differ only in their start-address field (address >> 4).
+      const uint64_t q_desc0 = umma_desc(q_addr, 16, 1024);
+      const uint64_t k_desc0 = umma_desc(slot_addr, 16, 1024);
+      const uint64_t v_desc0 = umma_desc(slot_addr, kTcHalfBytes, 1024);
+      auto issue_qk = [&](int j) {
+        const uint64_t kd = k_desc0 + (uint64_t)((((2 * j) % kTcSlots) * kTcSlotBytes) >> 4);
+        const uint32_t d = tbase + kColS + (uint32_t)(j & 1) * 128;
+        umma_ss(d, q_desc0, kd, kIdescQK, 0u);
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t off = (uint32_t)(kk >> 2) * 16384 + (uint32_t)(kk & 3) * 32;
-          umma_ss(d, umma_desc(q_addr + off, 16, 1024), umma_desc(kb + off, 16, 1024), kIdescQK,
-                  kk > 0);
+        for (int kk = 1; kk < 8; ++kk) {
+          const uint64_t off = (uint64_t)(((kk >> 2) * kTcHalfBytes + (kk & 3) * 32) >> 4);
+          const uint64_t qoff = (uint64_t)(((kk >> 2) * (kTcQBytes / 2) + (kk & 3) * 32) >> 4);
+          umma_ss(d, q_desc0 + qoff, kd + off, kIdescQK, 1u);
         }
         umma_commit(&bars.s_full[j & 1]);
-        umma_commit(&bars.kv_empty[s]);
-        return true;
+        umma_commit(&bars.kv_empty[(2 * j) % kTcSlots]);
       };
-      if (ok) ok = issue_qk(0);
-      for (int j = 0; ok && j < ntiles; ++j) {
-        if (j + 1 < ntiles && !issue_qk(j + 1)) break;
-        if (!TCW(4, mbar_wait(&bars.p_full[j & 1], (j >> 1) & 1, abort, a.err))) break;
-        const int s = (2 * j + 1) % kTcSlots;
-        if (!TCW(5, mbar_wait(&bars.kv_full[s], ((2 * j + 1) / kTcSlots) & 1, abort, a.err))) break;
+      auto wait_k = [&](int j) {
+        return TCW(2, mbar_wait(&bars.kv_full[(2 * j) % kTcSlots], ((2 * j) / kTcSlots) & 1, abort, a.err));
+      };
+      bool ok = mbar_wait(&bars.q_ready, 0, abort, a.err) && wait_k(0);
+      if (ok) {
         tc_fence_after();
-        const uint32_t vb = slot_addr + s * kTcSlotBytes;
-        const uint32_t p_tmem = tbase + (uint32_t)(j & 1) * 128;
+        issue_qk(0);
+      }
+      for (int j = 0; ok && j < ntiles; ++j) {
+        // S buffer (j+1)&1 last held S_{j-1}, consumed before P_{j-1} was
+        // signalled, which this thread waited for in the previous iteration.
+        if (j + 1 < ntiles) {
+          if (!wait_k(j + 1)) break;
+          tc_fence_after();
+          issue_qk(j + 1);
+        }
+        if (!TCW(4, mbar_wait(&bars.p_full, j & 1, abort, a.err))) break;
+        const int sv = (2 * j + 1) % kTcSlots;
+        if (!TCW(5, mbar_wait(&bars.kv_full[sv], ((2 * j + 1) / kTcSlots) & 1, abort, a.err))) break;
+        tc_fence_after();
+        const uint64_t vd = v_desc0 + (uint64_t)((sv * kTcSlotBytes) >> 4);
+        const uint32_t d = tbase + kColO;
+        umma_ts(d, tbase + kColP, vd, kIdescPV, j > 0 ? 1u : 0u);
 #pragma unroll
-        for (int half = 0; half < 2; ++half)
-#pragma unroll
-          for (int kt = 0; kt < 8; ++kt)
-            umma_ts(o_tmem, p_tmem + half * 64 + kt * 8, umma_desc(vb + kt * 2048, 16384, 1024),
-                    kIdescPV, (j > 0 || half > 0 || kt > 0) ? 1u : 0u);
-        umma_commit(&bars.kv_empty[s]);
+        for (int st = 1; st < 2 * (kTcTok / 16); ++st) {
+          const int part = st / (kTcTok / 16), kt = st % (kTcTok / 16);
+          umma_ts(d, tbase + kColP + part * 64 + kt * 8, vd + (uint64_t)((kt * 2048) >> 4), kIdescPV, 1u);
+        }
         umma_commit(&bars.o_done);
+        umma_commit(&bars.kv_empty[sv]);
       }
     }
   } else {
     // ------------------------------------------------------------- softmax
     const int quarter = warp & 3;           // TMEM lanes [32*quarter, +32)
+    const int half = (warp - 2) >> 2;       // column half: warps 2-5 -> 0, 6-9 -> 1
     const int r = quarter * 32 + lane;      // query row of this thread
     const uint32_t lane_base = tbase + ((uint32_t)(quarter * 32) << 16);
-    // Q row r into the 128-byte-swizzled K-major tile.
+    const uint32_t p_hi = lane_base + kColP + half * 32, p_lo = p_hi + 64;
+    const uint32_t o_col = lane_base + kColO + half * 64;
+    // Q rows: the two threads of a row each copy one 64-dim half of it into
+    // the 128-byte-swizzled K-major tile.
     {
       const bool live = r < it.nrows;
       const uint4* src = nullptr;
@@ -275,60 +314,78 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                                              ((size_t)qid * a.Hq + hq) * 128);
       }
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {
+      for (int c8 = 0; c8 < 8; ++c8) {
+        const int c = half * 8 + c8;
         const uint4 v = live ? src[c] : make_uint4(0, 0, 0, 0);
-        *reinterpret_cast<uint4*>(q_s + (c >> 3) * 16384 + r * 128 + (((c & 7) ^ (r & 7)) << 4)) = v;
+        *reinterpret_cast<uint4*>(q_s + half * (kTcQBytes / 2) + r * 128 + ((c8 ^ (r & 7)) << 4)) = v;
       }
       fence_proxy_async_smem();
-      mbar_arrive(&bars.q_ready);
+      if (half == 0) {
+        // one arrival per row, after both halves are written
+        pair_sync(quarter);
+        mbar_arrive(&bars.q_ready);
+      } else {
+        pair_sync(quarter);
+      }
     }
     float m_used = -INFINITY, l = 0.f;
     for (int j = 0; j < ntiles; ++j) {
       bool ok = TCW(0, mbar_wait(&bars.s_full[j & 1], (j >> 1) & 1, abort, a.err));
       tc_fence_after();
-      const int valid = (j == ntiles - 1) ? (npages - 8 * j - 1) * kPageSize + it.last_valid : kTcTok;
-      const uint32_t sb = lane_base + (uint32_t)(j & 1) * 128;
-      float s[128];
+      TCP_START(tp)
+      const int valid = (j == ntiles - 1) ? (npages - kTcPagesPerTile * j - 1) * kPageSize + it.last_valid
+                                          : kTcTok;
+      const int vh = valid - half * 64;      // valid columns in this thread's half
+      float s[64];
       {
         float t[32];
+        const uint32_t sb = lane_base + kColS + (uint32_t)(j & 1) * 128 + half * 64;
+        tmem_ld32(sb, t);
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          tmem_ld32(sb + c * 32, t);
-          tmem_wait_ld();
+        for (int i = 0; i < 32; ++i) s[i] = t[i];
+        tmem_ld32(sb + 32, t);
+        tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) s[c * 32 + i] = t[i];
-        }
+        for (int i = 0; i < 32; ++i) s[32 + i] = t[i];
       }
+      TCP_MARK(0, tp)
       // Max on the raw scores (the scale is positive), masked only on the
-      // partial last tile.
-      if (valid < kTcTok) {
+      // partial last tile; then exchange with the thread of the other half.
+      if (vh < 64) {
 #pragma unroll
-        for (int i = 0; i < 128; ++i)
-          if (i >= valid) s[i] = -INFINITY;
+        for (int i = 0; i < 64; ++i)
+          if (i >= vh) s[i] = -INFINITY;
       }
       float mr0 = s[0], mr1 = s[1];
 #pragma unroll
-      for (int i = 2; i < 128; i += 2) {
+      for (int i = 2; i < 64; i += 2) {
         mr0 = fmaxf(mr0, s[i]);
         mr1 = fmaxf(mr1, s[i + 1]);
       }
-      float mt = fmaxf(mr0, mr1) * a.scale_log2;
+      bars.xmax[j & 1][half][r] = fmaxf(mr0, mr1);
+      pair_sync(quarter);
+      float mt = fmaxf(bars.xmax[j & 1][0][r], bars.xmax[j & 1][1][r]) * a.scale_log2;
       if (!ok) mt = m_used;
-      // Warp-uniform decision (tcgen05.ld/st are warp-collective).
+      TCP_MARK(1, tp)
+      // PV of the previous tile must be done before P is overwritten and
+      // before O is rescaled. Both threads of a row take the same decision
+      // (same data), and __any_sync covers the same rows in both warps.
+      bool prev_done = (j == 0);
       if (__any_sync(0xffffffffu, mt > m_used + kRescaleThreshold)) {
         const float m_new = fmaxf(m_used, mt);
         const float f = fast_exp2(m_used - m_new);  // 0 when m_used is -inf
         if (j > 0) {
           if (!TCW(1, mbar_wait(&bars.o_done, (j - 1) & 1, abort, a.err))) ok = false;
+          prev_done = true;
           tc_fence_after();
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
+          for (int c = 0; c < 2; ++c) {
             float o[32];
-            tmem_ld32(lane_base + 256 + c * 32, o);
+            tmem_ld32(o_col + c * 32, o);
             tmem_wait_ld();
 #pragma unroll
             for (int i = 0; i < 32; ++i) o[i] *= f;
-            tmem_st32(lane_base + 256 + c * 32, o);
+            tmem_st32(o_col + c * 32, o);
           }
         }
         l *= f;
@@ -337,26 +394,37 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       float sum0 = 0.f, sum1 = 0.f;
       const float neg_m = -m_used;
 #pragma unroll
-      for (int i = 0; i < 128; i += 2) {
+      for (int i = 0; i < 64; i += 2) {
         s[i] = fast_exp2(fmaf(s[i], a.scale_log2, neg_m));  // masked: exp2(-inf) = 0
         s[i + 1] = fast_exp2(fmaf(s[i + 1], a.scale_log2, neg_m));
         sum0 += s[i];
         sum1 += s[i + 1];
       }
       l += sum0 + sum1;
+      TCP_MARK(2, tp)
+      if (!prev_done) {
+        if (!TCW(1, mbar_wait(&bars.o_done, (j - 1) & 1, abort, a.err))) ok = false;
+        tc_fence_after();
+      }
+      TCP_MARK(3, tp)
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
         uint32_t hi[16], lo[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) split_bf16x2(s[c * 32 + 2 * i], s[c * 32 + 2 * i + 1], hi[i], lo[i]);
-        tmem_st16u(sb + c * 16, hi);
-        tmem_st16u(sb + 64 + c * 16, lo);
+        tmem_st16u(p_hi + c * 16, hi);
+        tmem_st16u(p_lo + c * 16, lo);
       }
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&bars.p_full[j & 1]);
+      mbar_arrive(&bars.p_full);
+      TCP_MARK(4, tp)
     }
-    // Epilogue: normalised O row and log2-domain LSE into the partial slot.
+    // Epilogue: combine the two partial sums, then each thread writes its
+    // half of the normalised O row; the half-0 thread writes the LSE.
+    bars.xsum[half][r] = l;
+    pair_sync(quarter);
+    const float L = bars.xsum[0][r] + bars.xsum[1][r];
     const bool live = r < it.nrows;
     int64_t slot = 0;
     if (live) {
@@ -368,31 +436,35 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mbar_wait(&bars.o_done, (ntiles - 1) & 1, abort, a.err);
       tc_fence_after();
     }
-    const float inv = l > 0.f ? 1.f / l : 0.f;
+    const float inv = L > 0.f ? 1.f / L : 0.f;
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
+    for (int c = 0; c < 2; ++c) {
       float o[32];
       if (ntiles > 0) {
-        tmem_ld32(lane_base + 256 + c * 32, o);
+        tmem_ld32(o_col + c * 32, o);
         tmem_wait_ld();
       } else {
 #pragma unroll
         for (int i = 0; i < 32; ++i) o[i] = 0.f;
       }
       if (live) {
-        float4* dst = reinterpret_cast<float4*>(a.part_o + slot * 128 + c * 32);
+        float4* dst = reinterpret_cast<float4*>(a.part_o + slot * 128 + half * 64 + c * 32);
 #pragma unroll
         for (int i = 0; i < 8; ++i)
           dst[i] = make_float4(o[4 * i] * inv, o[4 * i + 1] * inv, o[4 * i + 2] * inv, o[4 * i + 3] * inv);
       }
     }
-    if (live) a.part_lse[slot] = l > 0.f ? m_used + log2f(l) : -INFINITY;
+    if (live && half == 0) a.part_lse[slot] = L > 0.f ? m_used + log2f(L) : -INFINITY;
   }
 #ifdef DD_EXPERIMENT_TIMING
   if (lane == 0)
     for (int k = 0; k < 8; ++k)
       if (tacc[k])
         atomicAdd(reinterpret_cast<unsigned long long*>(&a.err->pad[1]) + 8 + k, (unsigned long long)tacc[k]);
+  if (lane == 0)
+    for (int k = 0; k < 8; ++k)
+      if (tacc2[k])
+        atomicAdd(reinterpret_cast<unsigned long long*>(&a.err->pad[1]) + 16 + k, (unsigned long long)tacc2[k]);
 #endif
   tc_fence_before();
   __syncthreads();
@@ -405,6 +477,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
 int make_kv_tensor_map(CUtensorMap* map, const void* kv, int64_t num_pages, int Hkv, int D,
                        int elem_bytes, int two_halves);
+
+int tc_row_tile() { return kTcRows; }
 
 int launch_attn_tc(const AttnArgs& a, int64_t num_pages, int num_items, cudaStream_t st) {
   if (a.D != 128 || a.kv_dtype != DD_DTYPE_BF16 || a.q_dtype != DD_DTYPE_BF16)

@@ -12,6 +12,10 @@
 namespace dd {
 
 
+// One warp per (query, head). Lanes first fetch the slot ids and LSEs of up
+// to 32 path entries at once and reduce max / weights with shuffles; the
+// outputs are then accumulated with independent vector loads (lane owns E
+// consecutive elements), so no load waits on another.
 template <int D>
 __global__ void __launch_bounds__(256) merge_paths_kernel(MergeArgs a) {
   constexpr int E = D / 32;
@@ -27,35 +31,61 @@ __global__ void __launch_bounds__(256) merge_paths_kernel(MergeArgs a) {
   } else {
     n = a.nsplit;
   }
-  float m = -INFINITY, wsum = 0.f, acc[E];
+  float M = -INFINITY, W = 0.f, acc[E];
 #pragma unroll
   for (int e = 0; e < E; ++e) acc[e] = 0.f;
-  for (int i = 0; i < n; ++i) {
-    const int64_t slot = a.path_indptr ? (int64_t)a.path_slots[base + i] + h
-                                       : ((int64_t)i * a.batch + p) * a.Hq + h;
-    const float l = a.part_lse[slot];
-    if (l == -INFINITY) continue;
-    const float mn = fmaxf(m, l);
-    const float sa = exp2f(m - mn), sb = exp2f(l - mn);
-    const float* o = a.part_o + slot * D;
+  for (int c0 = 0; c0 < n; c0 += 32) {
+    const int i = c0 + lane;
+    int64_t slot = 0;
+    float l = -INFINITY;
+    if (i < n) {
+      slot = a.path_indptr ? (int64_t)a.path_slots[base + i] + h : ((int64_t)i * a.batch + p) * a.Hq + h;
+      l = a.part_lse[slot];
+    }
+    float cm = l;
 #pragma unroll
-    for (int e = 0; e < E; ++e) acc[e] = acc[e] * sa + o[lane + 32 * e] * sb;
-    wsum = wsum * sa + sb;
-    m = mn;
+    for (int o = 16; o > 0; o >>= 1) cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, o));
+    if (cm == -INFINITY) continue;  // nothing in this chunk
+    const float nm = fmaxf(M, cm);
+    const float f = exp2f(M - nm);  // 0 when M is -inf
+    M = nm;
+#pragma unroll
+    for (int e = 0; e < E; ++e) acc[e] *= f;
+    float w = l == -INFINITY ? 0.f : exp2f(l - M);
+    float ws = w;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ws += __shfl_xor_sync(0xffffffffu, ws, o);
+    W = W * f + ws;
+    const int cn = min(32, n - c0);
+#pragma unroll 4
+    for (int k = 0; k < cn; ++k) {
+      const float wk = __shfl_sync(0xffffffffu, w, k);
+      const int64_t sk = __shfl_sync(0xffffffffu, slot, k);
+      if (wk == 0.f) continue;
+      const float* o = a.part_o + sk * D + lane * E;
+      if (E == 4) {
+        const float4 v = *reinterpret_cast<const float4*>(o);
+        acc[0] += wk * v.x; acc[1] += wk * v.y; acc[2] += wk * v.z; acc[3] += wk * v.w;
+      } else {
+#pragma unroll
+        for (int e = 0; e < E; ++e) acc[e] += wk * o[e];
+      }
+    }
   }
   const int q = a.qorder ? a.qorder[p] : p;
-  const size_t ob = ((size_t)q * a.Hq + h) * D;
-  const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+  const size_t ob = ((size_t)q * a.Hq + h) * D + lane * E;
+  const float inv = W > 0.f ? 1.f / W : 0.f;
+  if (a.out_dtype == DD_DTYPE_F32) {
 #pragma unroll
-  for (int e = 0; e < E; ++e) {
-    const float v = acc[e] * inv;
-    if (a.out_dtype == DD_DTYPE_F32)
-      reinterpret_cast<float*>(a.out)[ob + lane + 32 * e] = v;
-    else
-      reinterpret_cast<__nv_bfloat16*>(a.out)[ob + lane + 32 * e] = __float2bfloat16_rn(v);
+    for (int e = 0; e < E; ++e) reinterpret_cast<float*>(a.out)[ob + e] = acc[e] * inv;
+  } else {
+#pragma unroll
+    for (int e = 0; e < E; e += 2)
+      *reinterpret_cast<uint32_t*>(reinterpret_cast<__nv_bfloat16*>(a.out) + ob + e) =
+          pack_bf16x2(acc[e] * inv, acc[e + 1] * inv);
   }
   if (a.lse && lane == 0)
-    a.lse[(size_t)q * a.Hq + h] = wsum > 0.f ? (m + log2f(wsum)) * kLn2 : -INFINITY;
+    a.lse[(size_t)q * a.Hq + h] = W > 0.f ? (M + log2f(W)) * kLn2 : -INFINITY;
 }
 
 cudaError_t launch_merge(const MergeArgs& a, cudaStream_t st) {
@@ -97,9 +127,8 @@ extern "C" int dd_merge_states(int32_t n, int32_t D, const float* oa, const floa
   if (n < 0 || D <= 0) return fail(DD_ERR_INVALID_ARGUMENT, "bad sizes");
   if (n == 0) return DD_OK;
   if (!oa || !la || !ob || !lb || !o || !l) return fail(DD_ERR_INVALID_ARGUMENT, "NULL pointer");
-  // Outputs may alias inputs: each element reads its inputs before writing,
-  // but lse is read by all D elements of a row, so go through a row-safe path
-  // when l aliases la/lb: compute into o first, then write lse in a second pass.
+  // o may alias oa or ob (each element reads its inputs before writing it),
+  // but every element of a row reads la/lb, so l may not alias them.
   const int64_t total = (int64_t)n * D;
   const int threads = 256;
   const int blocks = (int)((total + threads - 1) / threads);

@@ -85,6 +85,10 @@ static int kind_for(const dd_attn_config& c, const dd_plan_options& o, int64_t r
 
 static int row_tile_for(int kind) { return kind == kItemTc ? 128 : kind == kItemMma ? 16 : 64; }
 
+// SMs of the target GPU (B200); only a load-balancing heuristic, so the
+// planner needs no device.
+constexpr int kPlanSms = 148;
+
 namespace {
 
 struct TrieKey {
@@ -245,6 +249,14 @@ static void build_items(dd_plan* p) {
     int64_t chunk_pages = p->opts.max_chunk_pages > 0 ? p->opts.max_chunk_pages
                           : (row_tiles == 1 ? 16 : (int64_t)1 << 30);
     int64_t k = std::min<int64_t>(kmax, (n.page_count + chunk_pages - 1) / chunk_pages);
+    if (kind == kItemTc && p->opts.max_chunk_pages <= 0) {
+      // Wide nodes are compute-bound: split their pages so the tensor-core
+      // grid covers the SMs (at least 32 pages per chunk), even though each
+      // chunk adds a partial state per row.
+      const int64_t per = row_tiles * Hkv;
+      const int64_t target = std::max<int64_t>(1, (kPlanSms + per / 2) / per);
+      k = std::max<int64_t>(k, std::min<int64_t>({target, (int64_t)4, std::max<int64_t>(1, n.page_count / 32)}));
+    }
     k = std::max<int64_t>(1, std::min<int64_t>(k, n.page_count));
     for (int64_t ci = 0; ci < k; ++ci) {
       const int32_t pb = (int32_t)(ci * n.page_count / k);
