@@ -36,12 +36,16 @@ FALLBACK_HBM_GBS = 6650.0
 SEED = 0xD3D1
 
 
+FALLBACK_BF16_TFLOPS = 1590.0
+
+
 def peaks():
+    """(HBM GB/s, dense bf16 TFLOP/s burst, source)."""
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         d = json.loads(p.read_text())
-        return float(d["hbm_gbs"]), "measured"
-    return FALLBACK_HBM_GBS, "fallback"
+        return float(d["hbm_gbs"]), float(d.get("bf16_tflops", FALLBACK_BF16_TFLOPS)), "measured"
+    return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, "fallback"
 
 
 def dist_env():
@@ -211,7 +215,7 @@ def run_ours(args):
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     kv = WORKLOADS[args.workload]["kv"]
-    hbm_peak, peak_kind = peaks()
+    hbm_peak, tc_peak, peak_kind = peaks()
 
     tb = make_tree(args.workload, SEED + rank)
     Hq, Hkv, D, B = tb.num_qo_heads, tb.num_kv_heads, tb.head_dim, tb.batch_size
@@ -288,10 +292,27 @@ def run_ours(args):
         kv_bytes += 2 * Hkv * 4
     qo_bytes = B * Hq * D * 4
     eff_bytes = kv_bytes + qo_bytes
-    attn_kind = max(("attn_mma", "attn_tc", "attn_simple"), key=lambda k: prof[k][0])
-    attn_ms = prof[attn_kind][0] / max(prof[attn_kind][1], 1)
-    attn_bytes = kv_bytes + B * Hq * D * 2  # KV read once per tree node + queries
-    achieved = attn_bytes / (attn_ms * 1e-3) / 1e9
+    # Roofline of the dominant attention kernel: bytes (streaming kernels) or
+    # FLOPs (tcgen05 kernel) it is given by the plan, over its average launch.
+    kt = list(info.kv_tokens_by_kernel)
+    per_tok = 2 * Hkv * (D * elem + scale_bytes)
+    kernels = {}
+    for idx, name in ((0, "attn_simple"), (1, "attn_mma")):
+        if prof[name][1]:
+            ms_l = prof[name][0] / prof[name][1]
+            byts = kt[idx] * per_tok + (B * Hq * D * 2 if idx == 1 or not kt[1] else 0)
+            kernels[name] = {"bound": "hbm", "algorithmic": byts, "unit": "GB/s", "launch_ms": ms_l,
+                             "achieved": byts / (ms_l * 1e-3) / 1e9, "peak": hbm_peak}
+    if prof["attn_tc"][1]:
+        ms_l = prof["attn_tc"][0] / prof["attn_tc"][1]
+        flops = 4.0 * D * info.tc_row_tokens
+        kernels["attn_tc"] = {"bound": "tensor", "algorithmic": flops, "unit": "TFLOP/s",
+                              "launch_ms": ms_l, "achieved": flops / (ms_l * 1e-3) / 1e12,
+                              "peak": tc_peak}
+    for k in kernels.values():
+        k["frac"] = k["achieved"] / k["peak"]
+    attn_kind = max(kernels, key=lambda k: kernels[k]["launch_ms"] * prof[k][1])
+    dom = kernels[attn_kind]
     traffic = None
     tf = ROOT / "profiles" / "traffic.json"
     if tf.exists():
@@ -356,10 +377,12 @@ def run_ours(args):
                        "plan_nodes": info.num_nodes, "l2": "flushed between steps (256 MiB write, untimed)",
                        "parallelism": f"tree-partitioned x{world}"},
             "effective_gbs": gbs, "hbm_frac": gbs / hbm_peak,
-            "roofline": {"bound": "hbm", "kernel": attn_kind, "achieved": achieved, "peak": hbm_peak,
-                         "unit": "GB/s", "frac": achieved / hbm_peak, "traffic": traffic,
-                         "peak_source": peak_kind, "launch_ms": attn_ms,
-                         "algorithmic_bytes": attn_bytes},
+            "roofline": {"bound": dom["bound"], "kernel": attn_kind, "achieved": dom["achieved"],
+                         "peak": dom["peak"], "unit": dom["unit"], "frac": dom["frac"],
+                         "traffic": traffic, "peak_source": peak_kind + " (of measured)"
+                         if peak_kind == "measured" else "of fallback",
+                         "launch_ms": dom["launch_ms"], "algorithmic": dom["algorithmic"]},
+            "kernel_rooflines": kernels,
             "kernel_ms_per_step": {k: v[0] / max(prof_steps, 1) for k, v in prof.items() if v[1]},
             "cpu_baseline": cpu,
             "e2e": {"value": B * world / e2e_step_s, "unit": "queries/s",

@@ -367,37 +367,27 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
         kb = st;
         vb = st + kStepPages * C::kSliceRaw;
       } else {
-        // Dequantise the stage's codes into the warp's bf16 buffer.
-        for (int u = lane; u < np * 2 * kPageSize * (D / 16); u += 32) {
-          const int c = u % (D / 16);            // 16-code chunk along D
-          const int t = (u / (D / 16)) % kPageSize;
-          const int j = (u / (D / 16 * kPageSize)) % np;
-          const int kv = u / (D / 16 * kPageSize * np);
-          const uint8_t* src = st + (kv * kStepPages + j) * C::kSliceRaw + t * D +
-                               (((c & 7) ^ (t & 7)) << 4);
-          const uint4 codes = *reinterpret_cast<const uint4*>(src);
-          float scl;
-          if (KV == kKvE4m3) {
-            scl = kv ? sc_v : sc_k;
-          } else {
-            scl = e8m0_to_float(st[C::kRawStage + (kv * kStepPages + j) * C::kMxBytes +
-                                   t * (D / 32) + (c >> 1)]);
-          }
-          const uint32_t w[4] = {codes.x, codes.y, codes.z, codes.w};
-          uint32_t outw[8];
+        // Widen the stage's codes into the warp's bf16 buffer: per page
+        // slice 16 tokens x D/16 chunks of 16 codes, lane-strided.
+        for (int kv = 0; kv < 2; ++kv)
+          for (int j = 0; j < np; ++j) {
+            const uint8_t* src = st + (kv * kStepPages + j) * C::kSliceRaw;
+            const uint8_t* mx = st + C::kRawStage + (kv * kStepPages + j) * C::kMxBytes;
+            uint8_t* dst = conv + (kv * kStepPages + j) * C::kSliceBf16;
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const float2 f0 = e4m3x2_to_float2((uint16_t)(w[q] & 0xffff));
-            const float2 f1 = e4m3x2_to_float2((uint16_t)(w[q] >> 16));
-            outw[2 * q] = pack_bf16x2(f0.x * scl, f0.y * scl);
-            outw[2 * q + 1] = pack_bf16x2(f1.x * scl, f1.y * scl);
+            for (int i = 0; i < kPageSize * (D / 16) / 32; ++i) {
+              const int u = lane + 32 * i;
+              const int c = u % (D / 16), t = u / (D / 16);  // 16-code chunk along D, token
+              const uint4 codes =
+                  *reinterpret_cast<const uint4*>(src + t * D + (((c & 7) ^ (t & 7)) << 4));
+              // Per-head E4M3 scales are applied to the scores and the output.
+              const float mul = KV == kKvMx ? e8m0_to_float(mx[t * (D / 32) + (c >> 1)]) : (kv ? sc_v : sc_k);
+              uint32_t w[8];
+              e4m3x16_to_bf16(codes, mul, w);
+              *reinterpret_cast<uint4*>(dst + swz_bf16(t, 2 * c)) = make_uint4(w[0], w[1], w[2], w[3]);
+              *reinterpret_cast<uint4*>(dst + swz_bf16(t, 2 * c + 1)) = make_uint4(w[4], w[5], w[6], w[7]);
+            }
           }
-          uint8_t* dst = conv + (kv * kStepPages + j) * C::kSliceBf16;
-          *reinterpret_cast<uint4*>(dst + swz_bf16(t, 2 * c)) =
-              make_uint4(outw[0], outw[1], outw[2], outw[3]);
-          *reinterpret_cast<uint4*>(dst + swz_bf16(t, 2 * c + 1)) =
-              make_uint4(outw[4], outw[5], outw[6], outw[7]);
-        }
         __syncwarp();
         if (lane == 0) mbar_arrive(&sh.empty[s]);  // raw stage may be refilled
         kb = conv;

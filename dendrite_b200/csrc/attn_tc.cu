@@ -39,12 +39,29 @@ namespace dd {
 constexpr int kTcRows = 128;            // rows per item
 constexpr int kTcTok = 128;             // tokens per tile
 constexpr int kTcPagesPerTile = kTcTok / kPageSize;
-constexpr int kTcSlots = 5;             // K/V ring slots (32 KiB each)
-constexpr int kTcThreads = 320;
 constexpr int kTcSlotBytes = kTcTok * 128 * 2;   // 128 tokens x 128 dims bf16
 constexpr int kTcHalfBytes = kTcTok * 128;       // one 64-dim half of a slot
 constexpr int kTcQBytes = 128 * 128 * 2;
-constexpr int kTcSmem = kTcQBytes + kTcSlots * kTcSlotBytes + 1024;
+constexpr int kTcStages = 3;                     // FP8 staging ring (K or V tile each)
+constexpr int kTcStageCodes = kTcTok * 128;      // 128 tokens x 128 E4M3 codes
+constexpr int kTcStageExps = kTcPagesPerTile * 64;  // MXFP8 exponents of a staged tile
+// Staged codes keep the 128-byte swizzle of the TMA box, whose pattern
+// follows shared-memory address bits 7-9: every stage starts on 1 KiB, and
+// the exponents sit in their own area after the codes.
+constexpr int kTcStageBytes = kTcStageCodes + kTcStageExps;
+
+// Per KV dtype: bf16 pages are copied by TMA straight into the bf16 K/V ring;
+// FP8 pages (E4M3 codes) are copied into a staging ring and two converter
+// warps (10-11) widen them to bf16 in the ring's swizzled layout.
+template <int KV>
+struct TcCfg {
+  static constexpr bool kFp8 = KV != DD_DTYPE_BF16;
+  static constexpr int kSlots = kFp8 ? 4 : 5;    // K/V ring slots (32 KiB each)
+  static constexpr int kThreads = kFp8 ? 384 : 320;
+  static constexpr int kSmem =
+      kTcQBytes + kSlots * kTcSlotBytes + (kFp8 ? kTcStages * kTcStageBytes : 0) + 1024;
+};
+constexpr int kTcMaxSlots = 5;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0, kColP = 256, kColO = 384;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
@@ -143,8 +160,10 @@ __device__ __forceinline__ void tmem_st16u(uint32_t taddr, const uint32_t (&v)[1
 
 
 struct TcBars {
-  uint64_t kv_full[kTcSlots];
-  uint64_t kv_empty[kTcSlots];
+  uint64_t kv_full[kTcMaxSlots];
+  uint64_t kv_empty[kTcMaxSlots];
+  uint64_t st_full[kTcStages];   // FP8 staging: codes landed
+  uint64_t st_empty[kTcStages];  // FP8 staging: converted, reusable
   uint64_t s_full[2];
   uint64_t p_full;
   uint64_t o_done;
@@ -159,28 +178,37 @@ __device__ __forceinline__ void pair_sync(int quarter) {
   named_bar_sync(1 + quarter, 64);  // the two warps that share TMEM lanes of `quarter`
 }
 
-__global__ void __launch_bounds__(kTcThreads, 1)
+template <int KV>
+__global__ void __launch_bounds__(TcCfg<KV>::kThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap kv_map, AttnArgs a) {
+  constexpr int kTcSlots = TcCfg<KV>::kSlots;
+  constexpr bool kFp8 = TcCfg<KV>::kFp8;
   extern __shared__ uint8_t smem_raw[];
   __shared__ TcBars bars;
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   uint8_t* q_s = smem;                  // [2 dim-halves][128 rows][128 B]
   uint8_t* slots = smem + kTcQBytes;    // [slot][2 dim-halves][128 rows][128 B]
+  uint8_t* stages = slots + kTcSlots * kTcSlotBytes;  // FP8: [stage][128 rows][128 B]
+  uint8_t* stage_exps = stages + kTcStages * kTcStageCodes;  // [stage][8 pages][64 B]
 
   const WorkItem it = a.items[blockIdx.x];
   const uint32_t* pages = a.pages + it.page_off;
   const int npages = it.npages;
   const int ntiles = (npages + kTcPagesPerTile - 1) / kTcPagesPerTile;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#ifdef DD_EXPERIMENT_TIMING
   long long tacc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
   long long tacc2[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-  (void)tacc;
-  (void)tacc2;
+#endif
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kTcSlots; ++s) {
-      mbar_init(&bars.kv_full[s], 1);
+      mbar_init(&bars.kv_full[s], kFp8 ? 64 : 1);
       mbar_init(&bars.kv_empty[s], 1);
+    }
+    for (int s = 0; s < kTcStages; ++s) {
+      mbar_init(&bars.st_full[s], 1);
+      mbar_init(&bars.st_empty[s], 64);
     }
     mbar_init(&bars.s_full[0], 1);
     mbar_init(&bars.s_full[1], 1);
@@ -213,7 +241,47 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const bool mine = lane < kTcPagesPerTile;
     uint32_t cur = (mine && pj < npages) ? pages[pj] : 0xFFFFFFFFu;
     uint32_t nxt = 0xFFFFFFFFu;
-    for (int idx = 0; idx < 2 * ntiles; ++idx) {
+    for (int idx = 0; kFp8 && idx < 2 * ntiles; ++idx) {
+      // FP8: one box of [16 tokens][128 codes] per page into the staging ring,
+      // plus the page's 64 MXFP8 exponent bytes.
+      const int su = idx % kTcStages;
+      const int j = idx >> 1, kv = idx & 1;
+      if (kv == 0 && mine) {
+        const int pn = (j + 1) * kTcPagesPerTile + pj;
+        nxt = pn < npages ? pages[pn] : 0xFFFFFFFFu;
+      }
+      if (idx >= kTcStages &&
+          !mbar_wait(&bars.st_empty[su], ((idx / kTcStages) - 1) & 1, abort, a.err))
+        break;
+      const int present = min(kTcPagesPerTile, npages - j * kTcPagesPerTile);
+      if (lane == 0)
+        mbar_arrive_expect_tx(&bars.st_full[su],
+                              kTcStageCodes + (KV == DD_DTYPE_MXFP8 ? 64 * present : 0));
+      __syncwarp();
+      if (mine) {
+        uint8_t* dst = stages + su * kTcStageCodes;
+        int y = (int)rows_total;
+        bool ok_page = false;
+        if (cur != 0xFFFFFFFFu) {
+          if (cur < (uint32_t)a.num_pages) {
+            y = (int)((((int64_t)cur * 2 + kv) * a.Hkv + it.kv_head) * kPageSize);
+            ok_page = true;
+          } else {
+            report_error(a.err, kDevErrBadPage, cur);
+          }
+        }
+        tma_load_2d(dst + pj * 2048, &kv_map, 0, y, &bars.st_full[su]);
+        if (KV == DD_DTYPE_MXFP8 && pj < present) {
+          // A bad page id still delivers its 64 bytes (from page 0) so the
+          // transaction count completes; the error word marks the result.
+          const int64_t ys = ok_page ? y : (int64_t)kv * a.Hkv * kPageSize;
+          bulk_load(stage_exps + su * kTcStageExps + pj * 64,
+                    reinterpret_cast<const uint8_t*>(a.scales) + ys * 4, 64, &bars.st_full[su]);
+        }
+      }
+      if (kv == 1) cur = nxt;
+    }
+    for (int idx = 0; !kFp8 && idx < 2 * ntiles; ++idx) {
       const int s = idx % kTcSlots;
       const int j = idx >> 1, kv = idx & 1;
       if (kv == 0 && mine) {
@@ -293,6 +361,47 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         umma_commit(&bars.kv_empty[sv]);
       }
     }
+  } else if (kFp8 && warp >= 10) {
+    // ----------------------------------------------------------- converters
+    // Thread t of 64 widens chunks id = i*64 + t (i < 16) of each staged tile:
+    // chunk = 16 codes of one token (row), dims 16c..16c+15. Consecutive
+    // threads cover two rows x four chunks of one dim-half, so each quarter
+    // warp's two 16-byte stores hit eight distinct bank groups.
+    const int t = threadIdx.x - 320;
+    for (int idx = 0; idx < 2 * ntiles; ++idx) {
+      const int su = idx % kTcStages, s = idx % kTcSlots;
+      if (!mbar_wait(&bars.st_full[su], (idx / kTcStages) & 1, abort, a.err)) break;
+      if (idx >= kTcSlots &&
+          !mbar_wait(&bars.kv_empty[s], ((idx / kTcSlots) - 1) & 1, abort, a.err))
+        break;
+      const uint8_t* src = stages + su * kTcStageCodes;
+      const uint8_t* exps = stage_exps + su * kTcStageExps;
+      const float head_scale =
+          KV == DD_DTYPE_E4M3 ? reinterpret_cast<const float*>(a.scales)[(idx & 1) * a.Hkv + it.kv_head] : 1.f;
+      uint8_t* dst = slots + s * kTcSlotBytes;
+      // Rows of absent pages hold zero codes but no exponents.
+      const int live_rows = kPageSize * min(kTcPagesPerTile, npages - (idx >> 1) * kTcPagesPerTile);
+#pragma unroll 4
+      for (int i = 0; i < 16; ++i) {
+        const int id = i * 64 + t;
+        const int cl = id & 3, half = (id >> 3) & 1;
+        const int row = ((id >> 4) << 1) | ((id >> 2) & 1);
+        const int c = half * 4 + cl;
+        const uint4 codes = *reinterpret_cast<const uint4*>(src + row * 128 + ((c ^ (row & 7)) << 4));
+        // Dequantised values are rounded to bf16 (the reference dequantises
+        // pages to bf16 before attention).
+        float mul = head_scale;
+        if (KV == DD_DTYPE_MXFP8) mul = row < live_rows ? e8m0_to_float(exps[row * 4 + (c >> 1)]) : 1.f;
+        uint32_t o[8];
+        e4m3x16_to_bf16(codes, mul, o);
+        uint8_t* drow = dst + half * kTcHalfBytes + row * 128;
+        *reinterpret_cast<uint4*>(drow + (((2 * cl) ^ (row & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+        *reinterpret_cast<uint4*>(drow + (((2 * cl + 1) ^ (row & 7)) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(&bars.kv_full[s]);
+      mbar_arrive(&bars.st_empty[su]);
+    }
   } else {
     // ------------------------------------------------------------- softmax
     const int quarter = warp & 3;           // TMEM lanes [32*quarter, +32)
@@ -328,6 +437,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         pair_sync(quarter);
       }
     }
+    const float scale_log2 = a.scale_log2;
     float m_used = -INFINITY, l = 0.f;
     for (int j = 0; j < ntiles; ++j) {
       bool ok = TCW(0, mbar_wait(&bars.s_full[j & 1], (j >> 1) & 1, abort, a.err));
@@ -364,7 +474,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
       bars.xmax[j & 1][half][r] = fmaxf(mr0, mr1);
       pair_sync(quarter);
-      float mt = fmaxf(bars.xmax[j & 1][0][r], bars.xmax[j & 1][1][r]) * a.scale_log2;
+      float mt = fmaxf(bars.xmax[j & 1][0][r], bars.xmax[j & 1][1][r]) * scale_log2;
       if (!ok) mt = m_used;
       TCP_MARK(1, tp)
       // PV of the previous tile must be done before P is overwritten and
@@ -395,8 +505,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const float neg_m = -m_used;
 #pragma unroll
       for (int i = 0; i < 64; i += 2) {
-        s[i] = fast_exp2(fmaf(s[i], a.scale_log2, neg_m));  // masked: exp2(-inf) = 0
-        s[i + 1] = fast_exp2(fmaf(s[i + 1], a.scale_log2, neg_m));
+        s[i] = fast_exp2(fmaf(s[i], scale_log2, neg_m));  // masked: exp2(-inf) = 0
+        s[i + 1] = fast_exp2(fmaf(s[i + 1], scale_log2, neg_m));
         sum0 += s[i];
         sum1 += s[i + 1];
       }
@@ -480,20 +590,33 @@ int make_kv_tensor_map(CUtensorMap* map, const void* kv, int64_t num_pages, int 
 
 int tc_row_tile() { return kTcRows; }
 
+template <int KV>
+static cudaError_t launch_tc_t(const CUtensorMap& map, const AttnArgs& a, int num_items,
+                               cudaStream_t st) {
+  constexpr int smem = TcCfg<KV>::kSmem;
+  cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel<KV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       smem);
+  if (e != cudaSuccess) return e;
+  ProfScope ps(kProfTc, st);
+  attn_tc_kernel<KV><<<num_items, TcCfg<KV>::kThreads, smem, st>>>(map, a);
+  return cudaGetLastError();
+}
+
 int launch_attn_tc(const AttnArgs& a, int64_t num_pages, int num_items, cudaStream_t st) {
-  if (a.D != 128 || a.kv_dtype != DD_DTYPE_BF16 || a.q_dtype != DD_DTYPE_BF16)
-    return fail(DD_ERR_NOT_AVAILABLE, "tcgen05 path: bf16 KV and queries, head_dim 128");
+  const bool fp8 = a.kv_dtype == DD_DTYPE_E4M3 || a.kv_dtype == DD_DTYPE_MXFP8;
+  if (a.D != 128 || a.q_dtype != DD_DTYPE_BF16 || !(fp8 || a.kv_dtype == DD_DTYPE_BF16))
+    return fail(DD_ERR_NOT_AVAILABLE, "tcgen05 path: bf16/E4M3/MXFP8 KV, bf16 queries, head_dim 128");
+  if (a.kv_dtype == DD_DTYPE_MXFP8 && ((uintptr_t)a.scales & 15) != 0)
+    return fail(DD_ERR_INVALID_ARGUMENT, "MXFP8 kv_scales must be 16-byte aligned");
   CUtensorMap map;
-  int rc = make_kv_tensor_map(&map, a.kv, num_pages, a.Hkv, a.D, 2, 0);
+  int rc = make_kv_tensor_map(&map, a.kv, num_pages, a.Hkv, a.D, fp8 ? 1 : 2, 0);
   if (rc) return rc;
-  cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       kTcSmem);
-  if (e != cudaSuccess) return fail(DD_ERR_CUDA, std::string("attn_tc attribute: ") + cudaGetErrorString(e));
-  {
-    ProfScope ps(kProfTc, st);
-    attn_tc_kernel<<<num_items, kTcThreads, kTcSmem, st>>>(map, a);
+  cudaError_t e;
+  switch (a.kv_dtype) {
+    case DD_DTYPE_E4M3: e = launch_tc_t<DD_DTYPE_E4M3>(map, a, num_items, st); break;
+    case DD_DTYPE_MXFP8: e = launch_tc_t<DD_DTYPE_MXFP8>(map, a, num_items, st); break;
+    default: e = launch_tc_t<DD_DTYPE_BF16>(map, a, num_items, st); break;
   }
-  e = cudaGetLastError();
   if (e != cudaSuccess) return fail(DD_ERR_CUDA, std::string("attn_tc launch: ") + cudaGetErrorString(e));
   return DD_OK;
 }

@@ -78,6 +78,8 @@ struct dd_plan {
   int64_t num_slots = 0;
   int64_t kv_tokens = 0;
   int64_t kv_tokens_flat = 0;
+  int64_t kv_tokens_by_kind[dd::kNumItemKinds] = {0, 0, 0};
+  int64_t tc_row_tokens = 0;
   int32_t max_depth = 0;
   // Packed host image of everything the device needs, and its layout.
   std::vector<uint8_t> image;

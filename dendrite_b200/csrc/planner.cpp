@@ -77,7 +77,7 @@ namespace dd {
 static int kind_for(const dd_attn_config& c, const dd_plan_options& o, int64_t rows) {
   if (c.kv_dtype == DD_DTYPE_F32 || c.q_dtype != DD_DTYPE_BF16 || c.head_dim > 128)
     return kItemSimple;
-  if (o.use_tensor_cores && rows >= 128 && c.head_dim == 128 && c.kv_dtype == DD_DTYPE_BF16 &&
+  if (o.use_tensor_cores && rows >= 128 && c.head_dim == 128 && c.kv_dtype != DD_DTYPE_F32 &&
       dd_tc_available())
     return kItemTc;
   return kItemMma;
@@ -239,6 +239,8 @@ static void build_items(dd_plan* p) {
     const int64_t rows = (int64_t)n.num_q * g;
     const int kind = kind_for(c, p->opts, rows);
     const int rt = row_tile_for(kind);
+    p->kv_tokens_by_kind[kind] += n.num_tokens;
+    if (kind == kItemTc) p->tc_row_tokens += rows * n.num_tokens;
     const int64_t row_tiles = (rows + rt - 1) / rt;
     // Split-K chunking. Each extra chunk costs one more partial state per
     // (query, head) written and read back by the merge; allow at most 1/8 of
@@ -383,6 +385,8 @@ int dd_plan_get_info(const dd_plan* p, dd_plan_info* info) {
   info->max_depth = p->max_depth;
   info->kv_tokens = p->kv_tokens;
   info->kv_tokens_flat = p->kv_tokens_flat;
+  for (int k = 0; k < 3; ++k) info->kv_tokens_by_kernel[k] = p->kv_tokens_by_kind[k];
+  info->tc_row_tokens = p->tc_row_tokens;
   info->workspace_bytes = plan_workspace_bytes(p);
   info->device_bytes = p->image.size();
   return DD_OK;

@@ -133,6 +133,12 @@ typedef struct dd_plan_info {
   int64_t kv_tokens_flat;  /* tokens a non-sharing decode would read */
   size_t workspace_bytes;  /* required size of `workspace` */
   size_t device_bytes;     /* required size of the buffer given to dd_plan_upload */
+  /* Unique KV tokens read by each attention kernel: [0] CUDA-core kernel,
+   * [1] streaming tensor-core (mma) kernel, [2] tcgen05 kernel (wide nodes). */
+  int64_t kv_tokens_by_kernel[3];
+  /* Sum over tcgen05 nodes of (query rows x tokens): the kernel's
+   * 4 * head_dim FLOPs per unit (Q.K^T and P.V). */
+  int64_t tc_row_tokens;
 } dd_plan_info;
 
 int dd_plan_create(const dd_attn_config* cfg, int32_t batch_size,

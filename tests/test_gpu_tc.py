@@ -133,3 +133,39 @@ def test_mcts_subset_vs_oracle(cuda):
     ref, ref_lse = oracle.decode_batch(bits_to_f32(q), pool, tb.indptr, tb.block_ids, tb.num_tokens, 8)
     assert_close(got, bits_to_f32(bf16_bits(ref)), what="mcts128")
     np.testing.assert_allclose(lse, ref_lse, atol=2e-3)
+
+
+@pytest.mark.parametrize("fmt", ["e4m3", "mxfp8"])
+@pytest.mark.parametrize("prefix,gqa", [(1008, 0), (2050, 1)])
+def test_fp8_wide_root_vs_oracle(cuda, fmt, prefix, gqa):
+    """FP8 pages through tcgen05: codes widened to bf16 in shared memory (exact
+    for E4M3; per-head scales applied to S and O, MXFP8 exponents per element).
+    Compared with the oracle over the f32 dequantised pool at the bf16 bounds.
+    1008 tokens leave the last tile with one absent page; 2050 a 2-token page."""
+    tb = wl.build_tree("fp8wide", 32, 8, 128, prefix, [], 40, (1, 40), prefix)
+    rng = np.random.default_rng(prefix)
+    # No outliers here: x50 values make outputs of ~100, where one bf16 ulp
+    # (0.5) exceeds the absolute bound; the outlier case is covered by the
+    # FP8 tree test.
+    pool = bf16_bits(random_pool(rng, tb.num_pages, 8, 128))
+    q = bf16_bits(rng.standard_normal((tb.batch_size, 32, 128)).astype(np.float32))
+    codes, scales = dd.quantize_kv_pages(_dev_bf16(pool, cuda), fmt)
+    kvd = _lib.DTYPE_E4M3 if fmt == "e4m3" else _lib.DTYPE_MXFP8
+    cfg = dd.make_config(32, 8, 128, tb.num_pages, kv_dtype=kvd, gqa_map=gqa)
+    outs = {}
+    for tc in (True, False):
+        plan = dd.CascadePlan(cfg, tb.indptr, tb.block_ids, tb.num_tokens, use_tensor_cores=tc)
+        plan.upload(cuda)
+        _lib.profile_enable(True)
+        out, lse = dd.cascade_decode(cfg, plan, _dev_bf16(q, cuda), codes, scales)
+        torch.cuda.synchronize()
+        prof = _lib.profile_read()
+        _lib.profile_enable(False)
+        assert (prof["attn_tc"][1] == 1) == tc, prof
+        outs[tc] = (out.float().cpu().numpy(), lse.cpu().numpy())
+    deq = oracle.dequantize(codes.cpu().numpy(), scales.cpu().numpy(), fmt)
+    ref, ref_lse = oracle.decode_batch(bits_to_f32(q), deq, tb.indptr, tb.block_ids, tb.num_tokens, 8,
+                                       gqa_grouped=bool(gqa))
+    assert_close(outs[True][0], bits_to_f32(bf16_bits(ref)), what=f"{fmt} tc")
+    np.testing.assert_allclose(outs[True][1], ref_lse, atol=2e-3)
+    assert_close(outs[True][0], outs[False][0], what=f"{fmt} tc vs mma")
