@@ -86,6 +86,30 @@ extern "C" int dd_plan_upload(dd_plan* p, void* buf, size_t bytes, dd_stream_t s
   return DD_OK;
 }
 
+// One side stream and fork/join events per host thread and device: calls
+// from different threads never share events.
+struct SideStream {
+  cudaStream_t stream = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
+};
+
+static SideStream* side_stream() {
+  constexpr int kMaxDevices = 64;
+  thread_local SideStream per_dev[kMaxDevices];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  SideStream& s = per_dev[dev];
+  if (!s.stream) {
+    if (cudaStreamCreateWithFlags(&s.stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&s.fork, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&s.join, cudaEventDisableTiming) != cudaSuccess) {
+      s = SideStream{};
+      return nullptr;
+    }
+  }
+  return &s;
+}
+
 extern "C" int dd_cascade_decode(const dd_attn_config* cfg, const dd_plan* p, const void* q,
                                  const void* kv, const void* scales, void* out, float* lse,
                                  void* ws, size_t ws_bytes, dd_stream_t stream) {
@@ -108,21 +132,42 @@ extern "C" int dd_cascade_decode(const dd_attn_config* cfg, const dd_plan* p, co
   AttnArgs a = base_args(cfg, q, kv, scales, ws, (size_t)p->num_slots);
   a.pages = reinterpret_cast<const uint32_t*>(base + p->off_pages);
   a.qorder = reinterpret_cast<const int32_t*>(base + p->off_qorder);
+  // The tensor-core kernel (wide shared nodes, compute-bound) runs on a side
+  // stream forked from `st`, concurrently with the streaming kernel (narrow
+  // nodes, HBM-bound); the merge waits for both. The fork/join is a pair of
+  // events, so it also captures into a CUDA graph.
+  const int n_tc = (int)p->items[kItemTc].size();
+  const bool fork = n_tc > 0 && (!p->items[kItemMma].empty() || !p->items[kItemSimple].empty());
+  SideStream* side = nullptr;
+  if (fork) {
+    side = side_stream();
+    if (!side) return fail(DD_ERR_CUDA, "side stream creation failed");
+    e = cudaEventRecord(side->fork, st);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(side->stream, side->fork, 0);
+    if (e != cudaSuccess) return cuda_fail(e, "side stream fork");
+  }
+  if (n_tc) {
+    a.items = reinterpret_cast<const WorkItem*>(base + p->off_items[kItemTc]);
+    rc = launch_attn_tc(a, cfg->num_pages, n_tc, fork ? side->stream : st);
+    if (rc) return rc;
+  }
   for (int k = 0; k < kNumItemKinds; ++k) {
     const int n = (int)p->items[k].size();
-    if (!n) continue;
+    if (!n || k == kItemTc) continue;
     a.items = reinterpret_cast<const WorkItem*>(base + p->off_items[k]);
     if (k == kItemSimple) {
       e = launch_attn_simple(a, dim3(n), st);
       if (e != cudaSuccess) return cuda_fail(e, "attn_simple launch");
-    } else if (k == kItemMma) {
+    } else {
       a.num_items = n;
       rc = launch_attn_mma(a, cfg->num_pages, st);
       if (rc) return rc;
-    } else {
-      rc = launch_attn_tc(a, cfg->num_pages, n, st);
-      if (rc) return rc;
     }
+  }
+  if (fork) {
+    e = cudaEventRecord(side->join, side->stream);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(st, side->join, 0);
+    if (e != cudaSuccess) return cuda_fail(e, "side stream join");
   }
   MergeArgs m;
   m.part_o = a.part_o;

@@ -601,7 +601,10 @@ static cudaError_t launch_mma_t(const CUtensorMap& map, const AttnArgs& a, cudaS
   e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, attn_mma_kernel<D, KV>, kMmaThreads, smem);
   if (e != cudaSuccess) return e;
   const int ctas_needed = (a.num_items + kStreams - 1) / kStreams;
-  const int grid = std::max(1, std::min(ctas_needed, sms * std::max(per_sm, 1)));
+  int grid = std::max(1, std::min(ctas_needed, sms * std::max(per_sm, 1)));
+#ifdef DD_EXPERIMENT_MMA_GRID
+  if (const char* g = getenv("DD_MMA_GRID")) grid = std::max(1, std::min(grid, atoi(g)));
+#endif
   {
     ProfScope ps(kProfMma, st);
     attn_mma_kernel<D, KV><<<grid, kMmaThreads, smem, st>>>(map, a);

@@ -3,30 +3,35 @@
 // root and upper nodes of a tree, where hundreds to thousands of (query, GQA
 // head) rows read the same pages.
 //
-// One CTA per work item = (node, KV head, 128-row tile, page range):
+// One CTA per work item = (node, KV head, 256-row tile, page range). The rows
+// form two 128-row sub-tiles A and B that share every K/V tile:
 //   warp 0      TMA producer: K and V tiles of 128 tokens (8 pages x 2 boxes
-//               of [16 tokens][64 dims], 128-byte swizzle) into a 5-slot
+//               of [16 tokens][64 dims], 128-byte swizzle) into the K/V
 //               ring; lane p owns page p of each tile and reads its id one
-//               tile ahead;
+//               tile ahead. FP8 pages go to a staging ring instead and warps
+//               10-11 widen them to bf16 in the ring's layout.
 //   warp 1      allocates all 512 TMEM columns; lane 0 issues every
-//               tcgen05.mma and signals completion with tcgen05.commit:
-//                 S_j = Q . K_j^T   (A = Q, B = K tile, both K-major smem;
-//                                   S double-buffered, so Q.K_{j+1} runs
-//                                   while the softmax of tile j does)
-//                 O  += P_j . V_j   (A = P in TMEM, B = V tile MN-major)
-//   warps 2-9   softmax: each query row r (= TMEM lane r) is shared by two
-//               threads of two warps, one per 64-column half of the tile.
-//               Per tile they exchange only their partial row max through
-//               shared memory, keep the running max in the log2 domain and
-//               a partial sum each, write P as two bf16 terms (hi + lo, so
-//               P.V keeps ~16 significant bits of P) into the P columns, and
-//               rescale their half of the O row only when the max grows by
-//               more than 2^8 (otherwise the exponentials use the stale max,
-//               which is exact).
-// TMEM columns: S0 0-127, S1 128-255, P 256-383 (hi 256-319, lo 320-383),
-// O 384-511. Each tcgen05.mma costs the single issuing thread a fixed time,
-// so tiles are 128 tokens (N = 128) to keep that below the tensor work and
-// to amortise the shared-memory reads of the A operand.
+//               tcgen05.mma and signals completion with tcgen05.commit, per
+//               tile j in the order
+//                 P_A.V_j, Q_A.K_{j+1}, P_B.V_j, Q_B.K_{j+1}
+//               (S = Q.K^T: A = Q, B = K, both K-major smem; O += P.V: A = P
+//               in TMEM, B = V MN-major), so the tensor core works on one
+//               sub-tile while the softmax of the other runs (ping-pong).
+//   warps 2-9   softmax, one thread per row: warps 2-5 own sub-tile A, 6-9
+//               sub-tile B (a warp may only touch the TMEM lanes of its
+//               quarter, warp % 4). Per tile: row max (pass 1), then per
+//               64-token chunk exp2, row sum and P as two bf16 terms (hi +
+//               lo: P.V keeps ~16 significant bits of P) written over the
+//               chunk's own scores (pass 2). The running max is used lazily:
+//               O and the sum are rescaled only when the row max grows by
+//               more than 2^8, otherwise the exponentials keep the stale max,
+//               which is exact.
+// TMEM columns: A: S/P 0-127, O 128-255; B: S/P 256-383, O 384-511. P_j
+// overwrites S_j in place: S_{j+1} is committed after P.V_j, so when the
+// softmax sees S_{j+1} the previous P has been consumed and O is final for
+// a rescale. Each tcgen05.mma (M = N = 128, K = 16) occupies the tensor
+// pipe ~90 cycles, so a 256-row tile keeps it busy for 48 of them per
+// 128 tokens while each sub-tile's softmax has the other's 24 to run in.
 //
 // The arithmetic is ReferenceBackend::decode's
 // (crates/dendrite-core/src/attention/backend.rs:254-262) over the node's
@@ -36,12 +41,12 @@
 
 namespace dd {
 
-constexpr int kTcRows = 128;            // rows per item
+constexpr int kTcRows = 256;            // rows per item: two sub-tiles of 128
 constexpr int kTcTok = 128;             // tokens per tile
 constexpr int kTcPagesPerTile = kTcTok / kPageSize;
 constexpr int kTcSlotBytes = kTcTok * 128 * 2;   // 128 tokens x 128 dims bf16
 constexpr int kTcHalfBytes = kTcTok * 128;       // one 64-dim half of a slot
-constexpr int kTcQBytes = 128 * 128 * 2;
+constexpr int kTcQBytes = 128 * 128 * 2;         // one 128-row Q sub-tile
 constexpr int kTcStages = 3;                     // FP8 staging ring (K or V tile each)
 constexpr int kTcStageCodes = kTcTok * 128;      // 128 tokens x 128 E4M3 codes
 constexpr int kTcStageExps = kTcPagesPerTile * 64;  // MXFP8 exponents of a staged tile
@@ -56,14 +61,16 @@ constexpr int kTcStageBytes = kTcStageCodes + kTcStageExps;
 template <int KV>
 struct TcCfg {
   static constexpr bool kFp8 = KV != DD_DTYPE_BF16;
-  static constexpr int kSlots = kFp8 ? 4 : 5;    // K/V ring slots (32 KiB each)
+  static constexpr int kSlots = kFp8 ? 3 : 4;    // K/V ring slots (32 KiB each)
   static constexpr int kThreads = kFp8 ? 384 : 320;
   static constexpr int kSmem =
-      kTcQBytes + kSlots * kTcSlotBytes + (kFp8 ? kTcStages * kTcStageBytes : 0) + 1024;
+      2 * kTcQBytes + kSlots * kTcSlotBytes + (kFp8 ? kTcStages * kTcStageBytes : 0) + 1024;
 };
-constexpr int kTcMaxSlots = 5;
+constexpr int kTcMaxSlots = 4;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColS = 0, kColP = 256, kColO = 384;
+// Per sub-tile x: S (then P over it) at col_s(x), O at col_o(x).
+__device__ __forceinline__ uint32_t col_s(int x) { return (uint32_t)x * 256u; }
+__device__ __forceinline__ uint32_t col_o(int x) { return (uint32_t)x * 256u + 128u; }
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
 // Instruction descriptors, kind::f16, D f32, A/B bf16, M = 128, N = 128.
@@ -143,39 +150,73 @@ __device__ __forceinline__ void tmem_st16u(uint32_t taddr, const uint32_t (&v)[1
       : "memory");
 }
 
-// Wait-time accounting for pipeline experiments (off unless DD_EXPERIMENT_TIMING).
+// Wait-time and phase counters for pipeline experiments (compiled in only
+// with DD_EXPERIMENT_TIMING; summed into the workspace header's pad words).
 #ifdef DD_EXPERIMENT_TIMING
 #define TCW(slot, expr) ([&]() { const long long _t0 = clock64(); const bool _r = (expr); \
                                  tacc[slot] += clock64() - _t0; return _r; }())
-#else
-#define TCW(slot, expr) (expr)
-#endif
-#ifdef DD_EXPERIMENT_TIMING
 #define TCP_START(v) long long v = clock64();
 #define TCP_MARK(slot, v) { const long long _n = clock64(); tacc2[slot] += _n - v; v = _n; }
 #else
+#define TCW(slot, expr) (expr)
 #define TCP_START(v)
 #define TCP_MARK(slot, v)
 #endif
-
 
 struct TcBars {
   uint64_t kv_full[kTcMaxSlots];
   uint64_t kv_empty[kTcMaxSlots];
   uint64_t st_full[kTcStages];   // FP8 staging: codes landed
   uint64_t st_empty[kTcStages];  // FP8 staging: converted, reusable
-  uint64_t s_full[2];
-  uint64_t p_full;
-  uint64_t o_done;
-  uint64_t q_ready;
+  uint64_t s_full[2];            // per sub-tile: S_j ready (and P.V_{j-1} done)
+  uint64_t p_full[2];            // per sub-tile: P_j written (128 arrivals)
+  uint64_t o_done[2];            // per sub-tile: last P.V done
+  uint64_t q_ready;              // both Q sub-tiles in shared memory (256 arrivals)
   uint32_t tmem_base;
   int abort;
-  float xmax[2][2][128];  // [tile parity][column half][row]: partial row max
-  float xsum[2][128];     // [column half][row]: partial row sum (epilogue)
 };
 
-__device__ __forceinline__ void pair_sync(int quarter) {
-  named_bar_sync(1 + quarter, 64);  // the two warps that share TMEM lanes of `quarter`
+// 32 columns of this thread's TMEM lane, times f, written back.
+__device__ __forceinline__ void tmem_scale32(uint32_t taddr, float f) {
+  float o[32];
+  tmem_ld32(taddr, o);
+  tmem_wait_ld();
+#pragma unroll
+  for (int i = 0; i < 32; i += 2) {
+    const uint64_t v = f2_fma(f2_pack(o[i], o[i + 1]), f2_pack(f, f), 0ull);
+    o[i] = f2_lo(v);
+    o[i + 1] = f2_hi(v);
+  }
+  tmem_st32(taddr, o);
+}
+
+// Softmax of one 64-token chunk (s[], scores already masked): P = exp2(s *
+// scale - m), accumulated into *acc, written as bf16 hi / lo terms into the
+// chunk's own TMEM columns (hi: +0..31, lo: +32..63), which held its scores.
+__device__ __forceinline__ void softmax_chunk(float (&s)[64], uint64_t sc2, uint64_t nm2,
+                                              uint64_t& acc, uint32_t taddr) {
+  uint64_t a0 = 0ull, a1 = 0ull;
+#pragma unroll
+  for (int i = 0; i < 64; i += 4) {
+    const uint64_t x0 = f2_fma(f2_pack(s[i], s[i + 1]), sc2, nm2);
+    const uint64_t x1 = f2_fma(f2_pack(s[i + 2], s[i + 3]), sc2, nm2);
+    s[i] = fast_exp2(f2_lo(x0));
+    s[i + 1] = fast_exp2(f2_hi(x0));
+    s[i + 2] = fast_exp2(f2_lo(x1));
+    s[i + 3] = fast_exp2(f2_hi(x1));
+    a0 = f2_add(a0, f2_pack(s[i], s[i + 1]));
+    a1 = f2_add(a1, f2_pack(s[i + 2], s[i + 3]));
+  }
+  acc = f2_add(acc, f2_add(a0, a1));
+#pragma unroll
+  for (int c = 0; c < 2; ++c) {
+    uint32_t hi[16], lo[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+      split_bf16x2_packed(f2_pack(s[c * 32 + 2 * i], s[c * 32 + 2 * i + 1]), hi[i], lo[i]);
+    tmem_st16u(taddr + c * 16, hi);
+    tmem_st16u(taddr + 32 + c * 16, lo);
+  }
 }
 
 template <int KV>
@@ -186,8 +227,8 @@ __global__ void __launch_bounds__(TcCfg<KV>::kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   __shared__ TcBars bars;
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
-  uint8_t* q_s = smem;                  // [2 dim-halves][128 rows][128 B]
-  uint8_t* slots = smem + kTcQBytes;    // [slot][2 dim-halves][128 rows][128 B]
+  uint8_t* q_s = smem;                       // [sub-tile][2 dim-halves][128 rows][128 B]
+  uint8_t* slots = smem + 2 * kTcQBytes;     // [slot][2 dim-halves][128 rows][128 B]
   uint8_t* stages = slots + kTcSlots * kTcSlotBytes;  // FP8: [stage][128 rows][128 B]
   uint8_t* stage_exps = stages + kTcStages * kTcStageCodes;  // [stage][8 pages][64 B]
 
@@ -195,6 +236,7 @@ __global__ void __launch_bounds__(TcCfg<KV>::kThreads, 1)
   const uint32_t* pages = a.pages + it.page_off;
   const int npages = it.npages;
   const int ntiles = (npages + kTcPagesPerTile - 1) / kTcPagesPerTile;
+  const bool has_b = it.nrows > 128;  // second sub-tile in use
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 #ifdef DD_EXPERIMENT_TIMING
   long long tacc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
@@ -210,11 +252,12 @@ __global__ void __launch_bounds__(TcCfg<KV>::kThreads, 1)
       mbar_init(&bars.st_full[s], 1);
       mbar_init(&bars.st_empty[s], 64);
     }
-    mbar_init(&bars.s_full[0], 1);
-    mbar_init(&bars.s_full[1], 1);
-    mbar_init(&bars.p_full, 256);
-    mbar_init(&bars.o_done, 1);
-    mbar_init(&bars.q_ready, 128);
+    for (int x = 0; x < 2; ++x) {
+      mbar_init(&bars.s_full[x], 1);
+      mbar_init(&bars.p_full[x], 128);
+      mbar_init(&bars.o_done[x], 1);
+    }
+    mbar_init(&bars.q_ready, 256);
     bars.abort = 0;
     fence_mbar_init();
   }
@@ -309,56 +352,67 @@ __global__ void __launch_bounds__(TcCfg<KV>::kThreads, 1)
     }
   } else if (warp == 1) {
     // --------------------------------------------------------- MMA issuer
+    // Per tile j: P_A.V_j, Q_A.K_{j+1}, P_B.V_j, Q_B.K_{j+1}. Each P.V waits
+    // for its sub-tile's softmax, which overlaps the other sub-tile's products.
     if (lane == 0 && ntiles > 0) {
+      const int nsub = has_b ? 2 : 1;
       const uint32_t q_addr = smem_u32(q_s);
       const uint32_t slot_addr = smem_u32(slots);
       // Descriptors differ only in their start-address field (address >> 4).
       const uint64_t q_desc0 = umma_desc(q_addr, 16, 1024);
       const uint64_t k_desc0 = umma_desc(slot_addr, 16, 1024);
       const uint64_t v_desc0 = umma_desc(slot_addr, kTcHalfBytes, 1024);
-      auto issue_qk = [&](int j) {
+      auto issue_qk = [&](int x, int j) {
         const uint64_t kd = k_desc0 + (uint64_t)((((2 * j) % kTcSlots) * kTcSlotBytes) >> 4);
-        const uint32_t d = tbase + kColS + (uint32_t)(j & 1) * 128;
-        umma_ss(d, q_desc0, kd, kIdescQK, 0u);
+        const uint64_t qd = q_desc0 + (uint64_t)((x * kTcQBytes) >> 4);
+        const uint32_t d = tbase + col_s(x);
 #pragma unroll
-        for (int kk = 1; kk < 8; ++kk) {
+        for (int kk = 0; kk < 8; ++kk) {
           const uint64_t off = (uint64_t)(((kk >> 2) * kTcHalfBytes + (kk & 3) * 32) >> 4);
           const uint64_t qoff = (uint64_t)(((kk >> 2) * (kTcQBytes / 2) + (kk & 3) * 32) >> 4);
-          umma_ss(d, q_desc0 + qoff, kd + off, kIdescQK, 1u);
+          umma_ss(d, qd + qoff, kd + off, kIdescQK, kk > 0 ? 1u : 0u);
         }
-        umma_commit(&bars.s_full[j & 1]);
-        umma_commit(&bars.kv_empty[(2 * j) % kTcSlots]);
+        umma_commit(&bars.s_full[x]);
       };
-      auto wait_k = [&](int j) {
-        return TCW(2, mbar_wait(&bars.kv_full[(2 * j) % kTcSlots], ((2 * j) / kTcSlots) & 1, abort, a.err));
+      auto wait_slot = [&](int idx) {
+        return mbar_wait(&bars.kv_full[idx % kTcSlots], (idx / kTcSlots) & 1, abort, a.err);
       };
-      bool ok = mbar_wait(&bars.q_ready, 0, abort, a.err) && wait_k(0);
+      bool ok = mbar_wait(&bars.q_ready, 0, abort, a.err) && wait_slot(0);
       if (ok) {
         tc_fence_after();
-        issue_qk(0);
+        for (int x = 0; x < nsub; ++x) issue_qk(x, 0);
+        umma_commit(&bars.kv_empty[0]);
       }
       for (int j = 0; ok && j < ntiles; ++j) {
-        // S buffer (j+1)&1 last held S_{j-1}, consumed before P_{j-1} was
-        // signalled, which this thread waited for in the previous iteration.
-        if (j + 1 < ntiles) {
-          if (!wait_k(j + 1)) break;
-          tc_fence_after();
-          issue_qk(j + 1);
-        }
-        if (!TCW(4, mbar_wait(&bars.p_full, j & 1, abort, a.err))) break;
         const int sv = (2 * j + 1) % kTcSlots;
-        if (!TCW(5, mbar_wait(&bars.kv_full[sv], ((2 * j + 1) / kTcSlots) & 1, abort, a.err))) break;
-        tc_fence_after();
         const uint64_t vd = v_desc0 + (uint64_t)((sv * kTcSlotBytes) >> 4);
-        const uint32_t d = tbase + kColO;
-        umma_ts(d, tbase + kColP, vd, kIdescPV, j > 0 ? 1u : 0u);
+        for (int x = 0; ok && x < nsub; ++x) {
+          if (!TCW(4 - x, mbar_wait(&bars.p_full[x], j & 1, abort, a.err))) { ok = false; break; }
+          if (x == 0 && !TCW(5, wait_slot(2 * j + 1))) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t d = tbase + col_o(x);
 #pragma unroll
-        for (int st = 1; st < 2 * (kTcTok / 16); ++st) {
-          const int part = st / (kTcTok / 16), kt = st % (kTcTok / 16);
-          umma_ts(d, tbase + kColP + part * 64 + kt * 8, vd + (uint64_t)((kt * 2048) >> 4), kIdescPV, 1u);
+#ifdef DD_EXPERIMENT_NO_SPLIT
+          for (int st = 0; st < 8; ++st) {
+#else
+          for (int st = 0; st < 16; ++st) {
+#endif
+            const int kt = st & 7, part = st >> 3;  // hi terms, then lo terms
+            const uint32_t pa = tbase + col_s(x) + (kt >> 2) * 64 + part * 32 + (kt & 3) * 8;
+            umma_ts(d, pa, vd + (uint64_t)((kt * 2048) >> 4), kIdescPV, (j > 0 || st > 0) ? 1u : 0u);
+          }
+          if (j + 1 < ntiles) {
+            if (x == 0) {
+              if (!TCW(2, wait_slot(2 * j + 2))) { ok = false; break; }
+              tc_fence_after();
+            }
+            issue_qk(x, j + 1);
+            if (x == nsub - 1) umma_commit(&bars.kv_empty[(2 * j + 2) % kTcSlots]);
+          } else {
+            umma_commit(&bars.o_done[x]);
+          }
         }
-        umma_commit(&bars.o_done);
-        umma_commit(&bars.kv_empty[sv]);
+        if (ok) umma_commit(&bars.kv_empty[sv]);
       }
     }
   } else if (kFp8 && warp >= 10) {
@@ -402,179 +456,168 @@ __global__ void __launch_bounds__(TcCfg<KV>::kThreads, 1)
       mbar_arrive(&bars.kv_full[s]);
       mbar_arrive(&bars.st_empty[su]);
     }
-  } else {
+  } else if (warp >= 2 && warp < 10) {
     // ------------------------------------------------------------- softmax
+    const int x = (warp - 2) >> 2;          // sub-tile: warps 2-5 -> A, 6-9 -> B
     const int quarter = warp & 3;           // TMEM lanes [32*quarter, +32)
-    const int half = (warp - 2) >> 2;       // column half: warps 2-5 -> 0, 6-9 -> 1
-    const int r = quarter * 32 + lane;      // query row of this thread
+    const int r = quarter * 32 + lane;      // row within the sub-tile
+    const int row = x * 128 + r;            // row within the item
+    const bool live = row < it.nrows;
     const uint32_t lane_base = tbase + ((uint32_t)(quarter * 32) << 16);
-    const uint32_t p_hi = lane_base + kColP + half * 32, p_lo = p_hi + 64;
-    const uint32_t o_col = lane_base + kColO + half * 64;
-    // Q rows: the two threads of a row each copy one 64-dim half of it into
-    // the 128-byte-swizzled K-major tile.
+    const uint32_t s_col = lane_base + col_s(x);
+    const uint32_t o_col = lane_base + col_o(x);
+    // Q row -> the sub-tile's 128-byte-swizzled K-major tile.
     {
-      const bool live = r < it.nrows;
       const uint4* src = nullptr;
       if (live) {
-        const int rr = it.row0 + r, qi = rr / a.g;
+        const int rr = it.row0 + row, qi = rr / a.g;
         const int hq = qo_head_of(a.gqa_map, it.kv_head, rr % a.g, a.Hkv, a.g);
         const int qid = a.qorder ? a.qorder[it.q_begin + qi] : it.q_begin + qi;
         src = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(a.q) +
                                              ((size_t)qid * a.Hq + hq) * 128);
       }
+      uint8_t* qx = q_s + x * kTcQBytes + r * 128;
 #pragma unroll
-      for (int c8 = 0; c8 < 8; ++c8) {
-        const int c = half * 8 + c8;
+      for (int c = 0; c < 16; ++c) {
         const uint4 v = live ? src[c] : make_uint4(0, 0, 0, 0);
-        *reinterpret_cast<uint4*>(q_s + half * (kTcQBytes / 2) + r * 128 + ((c8 ^ (r & 7)) << 4)) = v;
+        *reinterpret_cast<uint4*>(qx + (c >> 3) * (kTcQBytes / 2) + (((c & 7) ^ (r & 7)) << 4)) = v;
       }
       fence_proxy_async_smem();
-      if (half == 0) {
-        // one arrival per row, after both halves are written
-        pair_sync(quarter);
-        mbar_arrive(&bars.q_ready);
-      } else {
-        pair_sync(quarter);
-      }
+      mbar_arrive(&bars.q_ready);
     }
+    const bool active = x == 0 || has_b;
     const float scale_log2 = a.scale_log2;
-    float m_used = -INFINITY, l = 0.f;
-    for (int j = 0; j < ntiles; ++j) {
-      bool ok = TCW(0, mbar_wait(&bars.s_full[j & 1], (j >> 1) & 1, abort, a.err));
+    float m_used = -INFINITY;
+    uint64_t lsum = 0ull;  // running row sum, as two packed partial sums
+    for (int j = 0; active && j < ntiles; ++j) {
+      bool ok = TCW(0, mbar_wait(&bars.s_full[x], j & 1, abort, a.err));
       tc_fence_after();
       TCP_START(tp)
+#ifdef DD_EXPERIMENT_NO_SOFTMAX
+      tc_fence_before();
+      mbar_arrive(&bars.p_full[x]);
+      continue;
+#endif
       const int valid = (j == ntiles - 1) ? (npages - kTcPagesPerTile * j - 1) * kPageSize + it.last_valid
                                           : kTcTok;
-      const int vh = valid - half * 64;      // valid columns in this thread's half
-      float s[64];
-      {
-        float t[32];
-        const uint32_t sb = lane_base + kColS + (uint32_t)(j & 1) * 128 + half * 64;
-        tmem_ld32(sb, t);
+      // Pass 1: row max of the raw scores (the scale is positive).
+      float mx = -INFINITY;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) s[i] = t[i];
-        tmem_ld32(sb + 32, t);
-        tmem_wait_ld();
+      for (int c = 0; c < 2; ++c) {
+        float s[64];
+        {
+          float t[32];
+          tmem_ld32(s_col + c * 64, t);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) s[32 + i] = t[i];
+          for (int i = 0; i < 32; ++i) s[i] = t[i];
+          tmem_ld32(s_col + c * 64 + 32, t);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) s[32 + i] = t[i];
+        }
+        const int vc = valid - c * 64;
+        if (vc < 64) {
+#pragma unroll
+          for (int i = 0; i < 64; ++i)
+            if (i >= vc) s[i] = -INFINITY;
+        }
+        float m0 = s[0], m1 = s[1];
+#pragma unroll
+        for (int i = 2; i < 62; i += 4) {
+          m0 = max3f(m0, s[i], s[i + 1]);
+          m1 = max3f(m1, s[i + 2], s[i + 3]);
+        }
+        mx = max3f(mx, max3f(m0, m1, s[62]), s[63]);
       }
-      TCP_MARK(0, tp)
-      // Max on the raw scores (the scale is positive), masked only on the
-      // partial last tile; then exchange with the thread of the other half.
-      if (vh < 64) {
-#pragma unroll
-        for (int i = 0; i < 64; ++i)
-          if (i >= vh) s[i] = -INFINITY;
-      }
-      float mr0 = s[0], mr1 = s[1];
-#pragma unroll
-      for (int i = 2; i < 64; i += 2) {
-        mr0 = fmaxf(mr0, s[i]);
-        mr1 = fmaxf(mr1, s[i + 1]);
-      }
-      bars.xmax[j & 1][half][r] = fmaxf(mr0, mr1);
-      pair_sync(quarter);
-      float mt = fmaxf(bars.xmax[j & 1][0][r], bars.xmax[j & 1][1][r]) * scale_log2;
+      float mt = mx * scale_log2;
       if (!ok) mt = m_used;
-      TCP_MARK(1, tp)
-      // PV of the previous tile must be done before P is overwritten and
-      // before O is rescaled. Both threads of a row take the same decision
-      // (same data), and __any_sync covers the same rows in both warps.
-      bool prev_done = (j == 0);
+      TCP_MARK(0, tp)
+      // Lazy rescale: the exponentials use a stale max unless the row max
+      // grew by more than 2^8. P.V_{j-1} is complete here (S_j was committed
+      // after it), so O can be rescaled in place; tcgen05.ld/st are warp-wide,
+      // hence the warp-uniform decision (a factor of 1 leaves a row as is).
       if (__any_sync(0xffffffffu, mt > m_used + kRescaleThreshold)) {
         const float m_new = fmaxf(m_used, mt);
         const float f = fast_exp2(m_used - m_new);  // 0 when m_used is -inf
         if (j > 0) {
-          if (!TCW(1, mbar_wait(&bars.o_done, (j - 1) & 1, abort, a.err))) ok = false;
-          prev_done = true;
-          tc_fence_after();
 #pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            float o[32];
-            tmem_ld32(o_col + c * 32, o);
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] *= f;
-            tmem_st32(o_col + c * 32, o);
-          }
+          for (int c = 0; c < 4; ++c) tmem_scale32(o_col + c * 32, f);
         }
-        l *= f;
+        lsum = f2_fma(lsum, f2_pack(f, f), 0ull);
         m_used = m_new;
       }
-      float sum0 = 0.f, sum1 = 0.f;
-      const float neg_m = -m_used;
-#pragma unroll
-      for (int i = 0; i < 64; i += 2) {
-        s[i] = fast_exp2(fmaf(s[i], scale_log2, neg_m));  // masked: exp2(-inf) = 0
-        s[i + 1] = fast_exp2(fmaf(s[i + 1], scale_log2, neg_m));
-        sum0 += s[i];
-        sum1 += s[i + 1];
-      }
-      l += sum0 + sum1;
-      TCP_MARK(2, tp)
-      if (!prev_done) {
-        if (!TCW(1, mbar_wait(&bars.o_done, (j - 1) & 1, abort, a.err))) ok = false;
-        tc_fence_after();
-      }
-      TCP_MARK(3, tp)
+      TCP_MARK(1, tp)
+      // Pass 2: exponentials, sum, P (hi, lo) over each chunk's own scores.
+      const uint64_t sc2 = f2_pack(scale_log2, scale_log2), nm2 = f2_pack(-m_used, -m_used);
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
-        uint32_t hi[16], lo[16];
+        float s[64];
+        {
+          float t[32];
+          tmem_ld32(s_col + c * 64, t);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) split_bf16x2(s[c * 32 + 2 * i], s[c * 32 + 2 * i + 1], hi[i], lo[i]);
-        tmem_st16u(p_hi + c * 16, hi);
-        tmem_st16u(p_lo + c * 16, lo);
+          for (int i = 0; i < 32; ++i) s[i] = t[i];
+          tmem_ld32(s_col + c * 64 + 32, t);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) s[32 + i] = t[i];
+        }
+        const int vc = valid - c * 64;
+        if (vc < 64) {
+#pragma unroll
+          for (int i = 0; i < 64; ++i)
+            if (i >= vc) s[i] = -INFINITY;
+        }
+        softmax_chunk(s, sc2, nm2, lsum, s_col + c * 64);
+        TCP_MARK(2 + c, tp)
       }
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&bars.p_full);
+      mbar_arrive(&bars.p_full[x]);
       TCP_MARK(4, tp)
     }
-    // Epilogue: combine the two partial sums, then each thread writes its
-    // half of the normalised O row; the half-0 thread writes the LSE.
-    bars.xsum[half][r] = l;
-    pair_sync(quarter);
-    const float L = bars.xsum[0][r] + bars.xsum[1][r];
-    const bool live = r < it.nrows;
-    int64_t slot = 0;
-    if (live) {
-      const int rr = it.row0 + r, qi = rr / a.g;
-      const int hq = qo_head_of(a.gqa_map, it.kv_head, rr % a.g, a.Hkv, a.g);
-      slot = (int64_t)it.slot_base + (int64_t)qi * a.Hq + hq;
-    }
-    if (ntiles > 0) {
-      mbar_wait(&bars.o_done, (ntiles - 1) & 1, abort, a.err);
-      tc_fence_after();
-    }
-    const float inv = L > 0.f ? 1.f / L : 0.f;
-#pragma unroll
-    for (int c = 0; c < 2; ++c) {
-      float o[32];
-      if (ntiles > 0) {
-        tmem_ld32(o_col + c * 32, o);
-        tmem_wait_ld();
-      } else {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) o[i] = 0.f;
-      }
+    // Epilogue: the normalised O row and its LSE.
+    if (active) {
+      const float L = f2_lo(lsum) + f2_hi(lsum);
+      int64_t slot = 0;
       if (live) {
-        float4* dst = reinterpret_cast<float4*>(a.part_o + slot * 128 + half * 64 + c * 32);
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-          dst[i] = make_float4(o[4 * i] * inv, o[4 * i + 1] * inv, o[4 * i + 2] * inv, o[4 * i + 3] * inv);
+        const int rr = it.row0 + row, qi = rr / a.g;
+        const int hq = qo_head_of(a.gqa_map, it.kv_head, rr % a.g, a.Hkv, a.g);
+        slot = (int64_t)it.slot_base + (int64_t)qi * a.Hq + hq;
       }
+      if (ntiles > 0) {
+        mbar_wait(&bars.o_done[x], 0, abort, a.err);
+        tc_fence_after();
+      }
+      const float inv = L > 0.f ? 1.f / L : 0.f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float o[32];
+        if (ntiles > 0) {
+          tmem_ld32(o_col + c * 32, o);
+          tmem_wait_ld();
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = 0.f;
+        }
+        if (live) {
+          float4* dst = reinterpret_cast<float4*>(a.part_o + slot * 128 + c * 32);
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+            dst[i] = make_float4(o[4 * i] * inv, o[4 * i + 1] * inv, o[4 * i + 2] * inv, o[4 * i + 3] * inv);
+        }
+      }
+      if (live) a.part_lse[slot] = L > 0.f ? m_used + log2f(L) : -INFINITY;
     }
-    if (live && half == 0) a.part_lse[slot] = L > 0.f ? m_used + log2f(L) : -INFINITY;
   }
 #ifdef DD_EXPERIMENT_TIMING
   if (lane == 0)
-    for (int k = 0; k < 8; ++k)
+    for (int k = 0; k < 8; ++k) {
       if (tacc[k])
         atomicAdd(reinterpret_cast<unsigned long long*>(&a.err->pad[1]) + 8 + k, (unsigned long long)tacc[k]);
-  if (lane == 0)
-    for (int k = 0; k < 8; ++k)
       if (tacc2[k])
         atomicAdd(reinterpret_cast<unsigned long long*>(&a.err->pad[1]) + 16 + k, (unsigned long long)tacc2[k]);
+    }
 #endif
   tc_fence_before();
   __syncthreads();

@@ -95,6 +95,42 @@ __device__ __forceinline__ void split_bf16x2(float a, float b, uint32_t& hi, uin
   lo = __byte_perm(__float_as_uint(ra), __float_as_uint(rb), 0x7632);
 }
 
+// Packed pair arithmetic (sm_100 f32x2 instructions: two lanes of f32 per
+// instruction) and a three-input max, for the softmax inner loops.
+__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
+  return ((uint64_t)__float_as_uint(b) << 32) | __float_as_uint(a);
+}
+__device__ __forceinline__ float f2_lo(uint64_t v) { return __uint_as_float((uint32_t)v); }
+__device__ __forceinline__ float f2_hi(uint64_t v) { return __uint_as_float((uint32_t)(v >> 32)); }
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// split_bf16x2 with the two subtractions as one packed instruction.
+__device__ __forceinline__ void split_bf16x2_packed(uint64_t ab, uint32_t& hi, uint32_t& lo) {
+  const uint32_t ua = (uint32_t)ab, ub = (uint32_t)(ab >> 32);
+  hi = __byte_perm(ua, ub, 0x7632);
+  const uint64_t r = f2_sub(ab, ((uint64_t)(ub & 0xffff0000u) << 32) | (ua & 0xffff0000u));
+  lo = __byte_perm((uint32_t)r, (uint32_t)(r >> 32), 0x7632);
+}
+
 // ------------------------------------------------------------------- timing
 __device__ __forceinline__ uint64_t global_ns() {
   uint64_t t;

@@ -83,7 +83,7 @@ static int kind_for(const dd_attn_config& c, const dd_plan_options& o, int64_t r
   return kItemMma;
 }
 
-static int row_tile_for(int kind) { return kind == kItemTc ? 128 : kind == kItemMma ? 16 : 64; }
+static int row_tile_for(int kind) { return kind == kItemTc ? 256 : kind == kItemMma ? 16 : 64; }
 
 // SMs of the target GPU (B200); only a load-balancing heuristic, so the
 // planner needs no device.
