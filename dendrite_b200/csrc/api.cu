@@ -137,7 +137,8 @@ extern "C" int dd_cascade_decode(const dd_attn_config* cfg, const dd_plan* p, co
   // nodes, HBM-bound); the merge waits for both. The fork/join is a pair of
   // events, so it also captures into a CUDA graph.
   const int n_tc = (int)p->items[kItemTc].size();
-  const bool fork = n_tc > 0 && (!p->items[kItemMma].empty() || !p->items[kItemSimple].empty());
+  const bool fork = n_tc > 0 && !prof_timing_on() &&
+                    (!p->items[kItemMma].empty() || !p->items[kItemSimple].empty());
   SideStream* side = nullptr;
   if (fork) {
     side = side_stream();

@@ -15,6 +15,9 @@ enum ProfKind {
 };
 void prof_begin(int kind, cudaStream_t st);
 void prof_end(int kind, cudaStream_t st);
+// True while per-launch timing is on: launches then run one at a time on
+// the caller's stream, so each event pair brackets one kernel alone.
+bool prof_timing_on();
 
 // RAII bracket around one launch.
 struct ProfScope {

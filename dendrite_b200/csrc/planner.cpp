@@ -89,32 +89,6 @@ static int row_tile_for(int kind) { return kind == kItemTc ? 256 : kind == kItem
 // planner needs no device.
 constexpr int kPlanSms = 148;
 
-namespace {
-
-struct TrieKey {
-  int32_t parent;
-  uint32_t page;
-  int32_t valid;
-  bool operator==(const TrieKey& o) const {
-    return parent == o.parent && page == o.page && valid == o.valid;
-  }
-};
-struct TrieKeyHash {
-  size_t operator()(const TrieKey& k) const {
-    uint64_t h = (uint64_t)(uint32_t)k.parent * 0x9E3779B97F4A7C15ull;
-    h ^= ((uint64_t)k.page << 5 | (uint64_t)k.valid) + 0x632BE59BD9B4E019ull + (h << 6) + (h >> 2);
-    return (size_t)(h ^ (h >> 29));
-  }
-};
-struct TrieNode {
-  uint32_t page = 0;
-  int32_t valid = 0;
-  std::vector<int32_t> children;
-  std::vector<int32_t> ends;  // queries whose table ends here
-};
-
-}  // namespace
-
 // Builds nodes / pages / query_order from the tables.
 static int build_nodes(dd_plan* p, const int32_t* indptr, const uint32_t* ids,
                        const int32_t* ntok) {
@@ -159,64 +133,113 @@ static int build_nodes(dd_plan* p, const int32_t* indptr, const uint32_t* ids,
     return DD_OK;
   }
 
-  // Trie over (page id, valid tokens) sequences. Node 0 is the empty root.
-  std::vector<TrieNode> trie(1);
-  std::unordered_map<TrieKey, int32_t, TrieKeyHash> index;
-  index.reserve((size_t)indptr[B] + 16);
+  // Radix tree over (page id, valid tokens) sequences. A node is a run of
+  // positions [off, off + len) of one source table; inserting a table walks
+  // runs with plain element compares and splits a run where the tables part.
+  struct Run {
+    int32_t q, off, len;          // source table and run within it
+    int32_t first_child = -1, last_child = -1, next_sibling = -1;
+    int32_t ends_head = -1, ends_tail = -1;  // queries whose table ends here
+  };
+  std::vector<Run> runs;
+  runs.reserve(2 * (size_t)B + 1);
+  runs.push_back(Run{-1, 0, 0});
+  std::vector<int32_t> end_next(B, -1);
+  auto key_eq = [&](int qa, int ia, int qb, int ib) {
+    return ids[indptr[qa] + ia] == ids[indptr[qb] + ib] && valid_of(qa, ia) == valid_of(qb, ib);
+  };
+  auto add_end = [&](int32_t n, int32_t b) {
+    if (runs[n].ends_tail < 0) runs[n].ends_head = b;
+    else end_next[runs[n].ends_tail] = b;
+    runs[n].ends_tail = b;
+  };
+  auto add_child = [&](int32_t n, int32_t c) {
+    if (runs[n].last_child < 0) runs[n].first_child = c;
+    else runs[runs[n].last_child].next_sibling = c;
+    runs[n].last_child = c;
+  };
   for (int b = 0; b < B; ++b) {
     int32_t cur = 0;
-    for (int i = 0; i < used[b]; ++i) {
-      TrieKey k{cur, ids[indptr[b] + i], valid_of(b, i)};
-      auto it = index.find(k);
-      if (it == index.end()) {
-        const int32_t nid = (int32_t)trie.size();
-        trie.emplace_back();
-        trie.back().page = k.page;
-        trie.back().valid = k.valid;
-        trie[cur].children.push_back(nid);
-        index.emplace(k, nid);
-        cur = nid;
-      } else {
-        cur = it->second;
+    int pos = 0;
+    for (;;) {
+      if (pos == used[b]) {
+        add_end(cur, b);
+        break;
       }
+      int32_t c = runs[cur].first_child;
+      while (c >= 0 && !key_eq(runs[c].q, runs[c].off, b, pos)) c = runs[c].next_sibling;
+      if (c < 0) {
+        const int32_t nid = (int32_t)runs.size();
+        runs.push_back(Run{b, pos, used[b] - pos});
+        add_child(cur, nid);
+        add_end(nid, b);
+        break;
+      }
+      const Run rc = runs[c];
+      const int lim = std::min(rc.len, used[b] - pos);
+      int k = 1;
+      {
+        // Ids first (contiguous compare), then the valid counts, which can
+        // differ only at either table's last page.
+        const uint32_t* x = ids + indptr[rc.q] + rc.off;
+        const uint32_t* y = ids + indptr[b] + pos;
+        while (k < lim && x[k] == y[k]) ++k;
+        for (int t = 1; t < k; ++t)
+          if (rc.off + t == used[rc.q] - 1 || pos + t == used[b] - 1)
+            if (valid_of(rc.q, rc.off + t) != valid_of(b, pos + t)) {
+              k = t;
+              break;
+            }
+      }
+      if (k < rc.len) {
+        // Split c after k positions: the tail keeps c's children and ends.
+        const int32_t tid = (int32_t)runs.size();
+        Run tail{rc.q, rc.off + k, rc.len - k};
+        tail.first_child = rc.first_child;
+        tail.last_child = rc.last_child;
+        tail.ends_head = rc.ends_head;
+        tail.ends_tail = rc.ends_tail;
+        runs.push_back(tail);
+        Run& head = runs[c];
+        head.len = k;
+        head.first_child = head.last_child = tid;
+        head.ends_head = head.ends_tail = -1;
+      }
+      pos += k;
+      cur = c;
     }
-    trie[cur].ends.push_back(b);
   }
 
-  // Iterative DFS that compresses single-child chains into nodes and emits
-  // queries in DFS order (queries ending at a trie node before its children).
+  // Pre-order DFS: one plan node per run, queries ending at a run emitted
+  // before its children's, so each node's queries are a contiguous range.
   p->query_order.reserve(B);
-  for (int32_t b : trie[0].ends) p->query_order.push_back(b);  // empty tables
+  for (int32_t b = runs[0].ends_head; b >= 0; b = end_next[b]) p->query_order.push_back(b);
   struct Frame {
-    int32_t node;        // plan node index (-1 for the root)
-    int32_t trie_end;    // trie node where this plan node ends
-    size_t next_child;   // next child of trie_end to descend into
+    int32_t node;   // plan node index (-1 for the root)
+    int32_t child;  // next child run to descend into
   };
   std::vector<Frame> stack;
-  stack.push_back({-1, 0, 0});
+  stack.push_back({-1, runs[0].first_child});
   while (!stack.empty()) {
     Frame& f = stack.back();
-    const TrieNode& tn = trie[f.trie_end];
-    if (f.next_child < tn.children.size()) {
-      const int32_t start = tn.children[f.next_child++];
+    if (f.child >= 0) {
+      const int32_t r = f.child;
+      f.child = runs[r].next_sibling;
+      const Run& rr = runs[r];
       Node n;
       n.parent = f.node;
       n.depth = f.node < 0 ? 0 : p->nodes[f.node].depth + 1;
       n.q_begin = (int32_t)p->query_order.size();
       n.page_off = (int32_t)p->pages.size();
-      int32_t t = start;
-      for (;;) {
-        p->pages.push_back(trie[t].page);
-        n.num_tokens += trie[t].valid;
-        n.last_valid = trie[t].valid;
-        if (trie[t].children.size() == 1 && trie[t].ends.empty()) t = trie[t].children[0];
-        else break;
-      }
-      n.page_count = (int32_t)p->pages.size() - n.page_off;
-      for (int32_t b : trie[t].ends) p->query_order.push_back(b);
+      n.page_count = rr.len;
+      const uint32_t* src = ids + indptr[rr.q] + rr.off;
+      p->pages.insert(p->pages.end(), src, src + rr.len);
+      n.num_tokens = (rr.len - 1) * kPageSize + valid_of(rr.q, rr.off + rr.len - 1);
+      n.last_valid = valid_of(rr.q, rr.off + rr.len - 1);
+      for (int32_t b = rr.ends_head; b >= 0; b = end_next[b]) p->query_order.push_back(b);
       p->nodes.push_back(n);
       p->max_depth = std::max(p->max_depth, n.depth + 1);
-      stack.push_back({(int32_t)p->nodes.size() - 1, t, 0});
+      stack.push_back({(int32_t)p->nodes.size() - 1, rr.first_child});
     } else {
       if (f.node >= 0) {
         Node& n = p->nodes[f.node];

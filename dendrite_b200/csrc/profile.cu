@@ -4,7 +4,8 @@
 // launch counter is always on (one relaxed atomic add); event timing is off
 // unless dd_profile_enable(1) was called, in which case an event pair is
 // recorded on the launching stream around each launch and resolved by
-// dd_profile_read.
+// dd_profile_read. While timing is on, dd_cascade_decode does not fork its
+// tensor-core kernel onto a side stream, so the pairs time kernels alone.
 #include <atomic>
 #include <mutex>
 #include <vector>
@@ -32,6 +33,8 @@ void prof_begin(int kind, cudaStream_t st) {
   cudaEventRecord(e, st);
   t_open[kind] = e;
 }
+
+bool prof_timing_on() { return g_prof_on.load(std::memory_order_relaxed) != 0; }
 
 void prof_end(int kind, cudaStream_t st) {
   if (!g_prof_on.load(std::memory_order_relaxed) || !t_open[kind]) return;
