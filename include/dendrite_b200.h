@@ -283,6 +283,19 @@ int dd_dequantize_kv_pages(const dd_quant_config* qc, const uint8_t* codes,
 int dd_scatter_head_shards(const dd_attn_config* cfg, int32_t world, int32_t batch_size,
                            const void* gathered, void* out, dd_stream_t stream);
 
+/* The collective of that split: ncclAllGather of this rank's local_out
+ * [batch][Hq/world][D] (cfg->q_dtype, bf16 or f32) into gathered (device
+ * scratch of world * batch * (Hq/world) * D elements) on `stream`, then
+ * dd_scatter_head_shards into out [batch][Hq][D]. nccl_comm is the caller's
+ * ncclComm_t over the `world` ranks (rank order = KV-head-group order); the
+ * library does not link NCCL, it calls the NCCL already loaded in the
+ * process (else libnccl.so.2), and returns DD_ERR_NOT_AVAILABLE without one.
+ * No reference counterpart: the reference has no multi-GPU attention; this is
+ * the all-gather its scope (one long tree split by KV-head group) calls for. */
+int dd_allgather_heads(void* nccl_comm, const dd_attn_config* cfg, int32_t world,
+                       int32_t batch_size, const void* local_out, void* gathered, void* out,
+                       dd_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
