@@ -1,19 +1,31 @@
 """Benchmark of the B200 cascade decode-attention path.
 
-Default workload (N=1): the MCTS-shaped Llama-3-8B tree — 32 query / 8 KV
-heads, head_dim 128, bf16 KV, an 8192-token root, shared nodes of 128-1024
-tokens at depths 1-3 (fan-out 8/4/4), 512 leaves with U[16, 256]-token
+Default workload (N=1): the MCTS-shaped Llama-3-8B tree (config 3) — 32 query
+/ 8 KV heads, head_dim 128, bf16 KV, an 8192-token root, shared nodes of
+128-1024 tokens at depths 1-3 (fan-out 8/4/4), 512 leaves with U[16, 256]-token
 private suffixes — one decode query per leaf. A step is one cascade decode of
 the whole batch (all 512 queries, every KV head) through dd_cascade_decode.
 
-With N GPUs (torchrun, one process per GPU) every rank decodes its own
-independent tree (trees are partitioned across GPUs; no collective on the data
-path), so scaling is weak and `value` = all ranks' queries / max-over-ranks
-time.
+Other workloads (--workload):
+  mcts8b-e4m3, mcts8b-mxfp8   config 4: config 3 over FP8 pages
+  forest70b                   config 5a: Llama-3-70B heads, 64 trees of a
+                              32768-token prefix + 64 x 256-token branches,
+                              trees partitioned across the ranks
+  long70b                     config 5b: one tree, 131072-token prefix + 256 x
+                              256-token branches, split by KV-head group across
+                              the ranks with an all-gather of the head outputs
+  quant-e4m3, quant-mxfp8     config 2: quantize a 4096-page x [2][4][16][64]
+                              bf16 pool (67.1 MB) with 0.1% x50 outliers
+
+Multi-GPU (torchrun, one process per GPU): mcts8b* give every rank its own
+tree (no collective; weak scaling); forest70b splits the 64 trees over the
+ranks (strong scaling, no collective); long70b splits the KV heads (strong
+scaling, one NCCL all-gather per step inside the timed region). `value` is
+the whole job's queries (or bytes) per second over the max-over-ranks time.
 
 Output: one JSON line (rank 0). `--impl reference` times the reference's CPU
-algorithm (the C restatement of ReferenceBackend::decode_batch in oracle/) on
-the host cores instead.
+algorithm (the C restatement of ReferenceBackend::decode_batch, or of the FP8
+quantizer, in oracle/) on the host cores instead.
 """
 from __future__ import annotations
 
@@ -32,11 +44,29 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 METRIC = "decode-attn queries/s + HBM GB/s (% of peak) at 1/2/4/8 B200, vs CPU reference"
+QUANT_METRIC = "KV-page quantize HBM GB/s (config 2), vs CPU reference"
 FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
 SEED = 0xD3D1
 
-
-FALLBACK_BF16_TFLOPS = 1590.0
+WORKLOADS = {
+    "mcts8b": dict(kind="tree", kv="bf16", tree="mcts", split="trees-per-rank",
+                   desc="config 3: Llama-3-8B heads, 8192 root, depths 1-3, 512 leaves"),
+    "mcts8b-e4m3": dict(kind="tree", kv="e4m3", tree="mcts", split="trees-per-rank",
+                        desc="config 4: config 3 with per-head E4M3 KV pages"),
+    "mcts8b-mxfp8": dict(kind="tree", kv="mxfp8", tree="mcts", split="trees-per-rank",
+                         desc="config 4: config 3 with MXFP8 KV pages"),
+    "forest70b": dict(kind="tree", kv="bf16", tree="forest", split="forest",
+                      desc="config 5a: Llama-3-70B heads, 64 trees x (32768 prefix + 64 x 256)"),
+    "long70b": dict(kind="tree", kv="bf16", tree="long", split="kv-heads",
+                    desc="config 5b: Llama-3-70B heads, one tree 131072 prefix + 256 x 256, "
+                         "KV-head split + all-gather"),
+    "quant-e4m3": dict(kind="quant", fmt="e4m3",
+                       desc="config 2: per-head E4M3 quantize of 4096 x [2][4][16][64] bf16 pages"),
+    "quant-mxfp8": dict(kind="quant", fmt="mxfp8",
+                        desc="config 2: MXFP8 quantize of 4096 x [2][4][16][64] bf16 pages"),
+}
+QUANT_PAGES, QUANT_HKV, QUANT_D = 4096, 4, 64
 
 
 def peaks():
@@ -55,17 +85,21 @@ def dist_env():
     return world, rank, local
 
 
-WORKLOADS = {
-    "mcts8b": dict(kv="bf16", desc="config 3: Llama-3-8B heads, 8192 root, depths 1-3, 512 leaves"),
-    "mcts8b-e4m3": dict(kv="e4m3", desc="config 4: config 3 with per-head E4M3 KV pages"),
-    "mcts8b-mxfp8": dict(kv="mxfp8", desc="config 4: config 3 with MXFP8 KV pages"),
-}
-
-
-def make_tree(name: str, seed: int):
+def make_tree(name: str, rank: int, world: int):
+    """This rank's tree batch and the job's total query count."""
     from dendrite_b200 import workloads as wl
 
-    return wl.mcts_llama3_8b(seed)
+    w = WORKLOADS[name]
+    if w["tree"] == "mcts":
+        tb = wl.mcts_llama3_8b(SEED + rank)
+        return tb, tb.batch_size * world
+    if w["tree"] == "forest":
+        if 64 % world:
+            raise SystemExit("forest70b splits 64 trees: world size must divide 64")
+        tb = wl.llama3_70b_forest(num_trees=64 // world, seed=SEED + rank)
+        return tb, tb.batch_size * world
+    tb = wl.llama3_70b_long(SEED)  # the same tree on every rank; heads are split
+    return tb, tb.batch_size
 
 
 class Clocks:
@@ -78,7 +112,6 @@ class Clocks:
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
         try:
-            self.f = open(out, "w") if out else subprocess.DEVNULL
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={device_index}", f"--query-gpu={q}", "--format=csv,noheader,nounits",
                  "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
@@ -110,28 +143,7 @@ class Clocks:
                 "samples": len(rows)}
 
 
-def cpu_sample_rate(tb, pool_bits, q_f32, budget_s: float, threads: int):
-    """Reference CPU algorithm (oracle restatement of ReferenceBackend::decode_batch)
-    on the first queries of the batch; returns (queries/s, n queries, seconds)."""
-    import oracle
-
-    def run(n):
-        ip = tb.indptr[: n + 1]
-        ids = tb.block_ids[: ip[-1]]
-        t0 = time.perf_counter()
-        oracle.decode_batch(q_f32[:n], pool_bits, ip, ids, tb.num_tokens[:n], tb.num_kv_heads,
-                            threads=threads)
-        return time.perf_counter() - t0
-
-    n = min(threads, tb.batch_size)
-    t = run(n)
-    per = t / n
-    n2 = int(max(n, min(tb.batch_size, budget_s / max(per, 1e-6))))
-    n2 = max(threads, (n2 // threads) * threads) if n2 >= threads else n2
-    t2 = run(n2)
-    return n2 / t2, n2, t2
-
-
+# ------------------------------------------------------------ CPU baselines
 def oracle_threads(tb) -> int:
     """Host threads for the CPU reference: all cores, capped by the memory its
     per-thread gather/repeat copies need."""
@@ -147,16 +159,72 @@ def oracle_threads(tb) -> int:
     return int(max(1, min(cores, avail * 0.5 // max(per, 1))))
 
 
-def host_workload(args, rank):
-    tb = make_tree(args.workload, SEED + rank)
-    rng = np.random.default_rng(SEED + rank)
+def cpu_sample_rate(tb, pool, q_f32, budget_s: float, threads: int):
+    """Reference CPU algorithm (oracle restatement of ReferenceBackend::decode_batch)
+    on the first queries of the batch; returns (queries/s, n queries, seconds)."""
     import oracle
 
+    def run(n):
+        ip = tb.indptr[: n + 1]
+        ids = tb.block_ids[: ip[-1]]
+        t0 = time.perf_counter()
+        oracle.decode_batch(q_f32[:n], pool, ip, ids, tb.num_tokens[:n], tb.num_kv_heads,
+                            threads=threads)
+        return time.perf_counter() - t0
+
+    n = min(threads, tb.batch_size)
+    t = run(n)
+    per = t / n
+    n2 = int(max(n, min(tb.batch_size, budget_s / max(per, 1e-6))))
+    n2 = max(threads, (n2 // threads) * threads) if n2 >= threads else n2
+    if n2 > n:
+        t = run(n2)
+    else:
+        n2 = n
+    return n2 / t, n2, t
+
+
+def host_tree_workload(name, rank, world):
+    import oracle
+
+    tb, _ = make_tree(name, rank, world)
+    rng = np.random.default_rng(SEED + rank)
     pool = oracle.f32_to_bf16_bits(
         rng.standard_normal((tb.num_pages, 2, tb.num_kv_heads, 16, tb.head_dim), dtype=np.float32))
     q = oracle.f32_to_bf16_bits(
         rng.standard_normal((tb.batch_size, tb.num_qo_heads, tb.head_dim), dtype=np.float32))
     return tb, pool, q
+
+
+def quant_pool_host(rank: int):
+    """Config 2 pool as bf16 bits: N(0,1) with 0.1% of the elements x50."""
+    import oracle
+
+    rng = np.random.default_rng(SEED + rank)
+    x = rng.standard_normal((QUANT_PAGES, 2, QUANT_HKV, 16, QUANT_D), dtype=np.float32)
+    x[rng.random(x.shape) < 1e-3] *= 50.0
+    return oracle.f32_to_bf16_bits(x)
+
+
+def quant_bytes(fmt: str) -> int:
+    """Algorithmic bytes of one config-2 quantize: bf16 pool read once, codes
+    written, E8M0 exponents (MXFP8) or 2 x Hkv scales (E4M3) written."""
+    n = QUANT_PAGES * 2 * QUANT_HKV * 16 * QUANT_D
+    return n * 2 + n + (n // 32 if fmt == "mxfp8" else 2 * QUANT_HKV * 4)
+
+
+def time_quant_cpu(pool_bits, fmt: str, budget_s: float):
+    import oracle
+
+    f = (lambda: oracle.quantize_per_head(pool_bits)) if fmt == "e4m3" else (lambda: oracle.quantize_mx(pool_bits))
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        f()
+        n += 1
+        if time.perf_counter() - t0 > budget_s or n >= 20:
+            break
+    return (time.perf_counter() - t0) / n, n
 
 
 def run_reference(args):
@@ -165,11 +233,27 @@ def run_reference(args):
         return
     import oracle
 
-    kv = WORKLOADS[args.workload]["kv"]
-    tb, pool, qbits = host_workload(args, 0)
-    if kv != "bf16":
-        codes, sc = (oracle.quantize_per_head(pool) if kv == "e4m3" else oracle.quantize_mx(pool))
-        pool = oracle.dequantize(codes, sc, kv)
+    w = WORKLOADS[args.workload]
+    base = {"impl": "reference", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "scaling": "weak", "vs_baseline": None, "data": "synthetic (seeded N(0,1))",
+            "config": {"workload": args.workload, "desc": w["desc"]}}
+    if w["kind"] == "quant":
+        pool = quant_pool_host(0)
+        for _ in range(min(args.warmup, 1)):
+            time_quant_cpu(pool, w["fmt"], 0.0)
+        per, n = time_quant_cpu(pool, w["fmt"], max(1.0, args.steps * 0.5))
+        gbs = quant_bytes(w["fmt"]) / per / 1e9
+        line = dict(base, metric=QUANT_METRIC, value=gbs, unit="GB/s", ms_per_step=per * 1e3,
+                    higher_is_better=True, dtype="bf16 -> e4m3",
+                    cpu_baseline={"value": gbs, "unit": "GB/s", "cores": 1, "kind": "port",
+                                  "sample": f"the whole config-2 pool, {n} runs (single-threaded C oracle)"},
+                    e2e={"value": gbs, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0})
+        print(json.dumps(line), flush=True)
+        return
+    tb, pool, qbits = host_tree_workload(args.workload, 0, 1)
+    if w["kv"] != "bf16":
+        codes, sc = (oracle.quantize_per_head(pool) if w["kv"] == "e4m3" else oracle.quantize_mx(pool))
+        pool = oracle.dequantize(codes, sc, w["kv"])
     q = oracle.bf16_bits_to_f32(qbits)
     threads = oracle_threads(tb)
     n = min(tb.batch_size, threads)
@@ -187,65 +271,23 @@ def run_reference(args):
     dt = time.perf_counter() - t0
     val = n * args.steps / dt
     sample = f"first {n} of {tb.batch_size} queries per step ({threads} threads), {args.steps} steps"
-    line = {
-        "impl": "reference", "metric": METRIC, "value": val, "unit": "queries/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic (seeded N(0,1))",
-        "config": {"workload": args.workload, "desc": WORKLOADS[args.workload]["desc"]},
-        "cpu_baseline": {"value": val, "unit": "queries/s", "cores": threads, "kind": "port",
-                         "sample": sample},
-        "e2e": {"value": val, "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }
+    line = dict(base, metric=METRIC, value=val, unit="queries/s", ms_per_step=dt / args.steps * 1e3,
+                higher_is_better=True, dtype="f32",
+                cpu_baseline={"value": val, "unit": "queries/s", "cores": threads, "kind": "port",
+                              "sample": sample},
+                e2e={"value": val, "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0})
     print(json.dumps(line), flush=True)
 
 
-def run_ours(args):
+# ------------------------------------------------------------------ timing
+def timed_steps(step, flush, args, world, rank, local, dev):
+    """W warm-up steps, then K steps each bracketed by CUDA events on the
+    current stream with an untimed L2 flush between them; barrier + sync on
+    both sides; max over ranks. Returns (ms per step, launches, clocks)."""
     import torch
     import torch.distributed as dist
 
-    import dendrite_b200 as dd
     from dendrite_b200 import _lib
-    from dendrite_b200 import workloads as wl
-
-    world, rank, local = dist_env()
-    if world > 1:
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
-    dev = torch.device("cuda", local)
-    torch.cuda.set_device(dev)
-    kv = WORKLOADS[args.workload]["kv"]
-    hbm_peak, tc_peak, peak_kind = peaks()
-
-    tb = make_tree(args.workload, SEED + rank)
-    Hq, Hkv, D, B = tb.num_qo_heads, tb.num_kv_heads, tb.head_dim, tb.batch_size
-    gen = torch.Generator(device=dev)
-    gen.manual_seed(SEED + rank)
-    pool = torch.randn((tb.num_pages, 2, Hkv, 16, D), generator=gen, device=dev,
-                       dtype=torch.float32).to(torch.bfloat16)
-    q = torch.randn((B, Hq, D), generator=gen, device=dev, dtype=torch.float32).to(torch.bfloat16)
-    scales = None
-    kv_dtype, elem, scale_bytes = _lib.DTYPE_BF16, 2.0, 0.0
-    if kv != "bf16":
-        codes, scales = dd.quantize_kv_pages(pool, kv)
-        kv_pages = codes
-        kv_dtype = _lib.DTYPE_E4M3 if kv == "e4m3" else _lib.DTYPE_MXFP8
-        elem = 1.0
-        scale_bytes = D / 32 if kv == "mxfp8" else 0.0
-    else:
-        kv_pages = pool
-    cfg = dd.make_config(Hq, Hkv, D, tb.num_pages, kv_dtype=kv_dtype)
-    plan = dd.CascadePlan(cfg, tb.indptr, tb.block_ids, tb.num_tokens)
-    plan.upload(dev)
-    info = plan.info()
-    ws = torch.empty(max(int(info.workspace_bytes), 256), dtype=torch.uint8, device=dev)
-    out = torch.empty_like(q)
-    lse = torch.empty(B, Hq, dtype=torch.float32, device=dev)
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # > 126 MB L2
-    stream = torch.cuda.current_stream()
-
-    def step():
-        dd.cascade_decode(cfg, plan, q, kv_pages, scales, out, lse, ws)
 
     for _ in range(args.warmup):
         step()
@@ -256,6 +298,7 @@ def run_ours(args):
     torch.cuda.synchronize()
     clocks = Clocks(local, ROOT / "gpurun_out" / f"clocks_rank{rank}.csv"
                     if (ROOT / "gpurun_out").is_dir() else None)
+    stream = torch.cuda.current_stream()
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
           for _ in range(args.steps)]
     n0 = _lib.launch_count()
@@ -274,33 +317,121 @@ def run_ours(args):
     t = torch.tensor([ms], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms_max = float(t.item())
-    ms_step = ms_max / args.steps
+    return float(t.item()) / args.steps, int(launches), clk
 
-    # Per-kernel durations (CUDA events on the launching stream), separate pass.
+
+def profile_kernels(step, flush, steps):
+    """Per-kernel CUDA-event durations; launches run one at a time in this mode."""
+    import torch
+
+    from dendrite_b200 import _lib
+
     _lib.profile_enable(True)
-    prof_steps = min(args.steps, 20)
-    for _ in range(prof_steps):
+    for _ in range(steps):
         step()
         flush.zero_()
     torch.cuda.synchronize()
     prof = _lib.profile_read()
     _lib.profile_enable(False)
+    return prof
 
-    kv_bytes = info.kv_tokens * 2 * Hkv * (D * elem + scale_bytes)
-    if kv == "e4m3":
-        kv_bytes += 2 * Hkv * 4
-    qo_bytes = B * Hq * D * 4
-    eff_bytes = kv_bytes + qo_bytes
+
+def e2e_time(e2e_step, args, world, dev):
+    import torch
+    import torch.distributed as dist
+
+    for _ in range(3):
+        e2e_step()
+    n = max(5, min(args.steps, 30))
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(n):
+        e2e_step()
+    t = torch.tensor([(time.perf_counter() - t0) / n], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def run_tree(args, world, rank, local, dev):
+    import torch
+    import torch.distributed as dist
+
+    import dendrite_b200 as dd
+    from dendrite_b200 import _lib
+    from dendrite_b200 import head_split as hs
+
+    w = WORKLOADS[args.workload]
+    kv = w["kv"]
+    heads = w["split"] == "kv-heads"
+    hbm_peak, tc_peak, peak_kind = peaks()
+
+    tb, total_queries = make_tree(args.workload, rank, world)
+    Hq, Hkv, D, B = tb.num_qo_heads, tb.num_kv_heads, tb.head_dim, tb.batch_size
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(SEED if heads else SEED + rank)
+    pool = torch.randn((tb.num_pages, 2, Hkv, 16, D), generator=gen, device=dev,
+                       dtype=torch.float32).to(torch.bfloat16)
+    q = torch.randn((B, Hq, D), generator=gen, device=dev, dtype=torch.float32).to(torch.bfloat16)
+    scales = None
+    kv_dtype, elem, scale_bytes = _lib.DTYPE_BF16, 2.0, 0.0
+    if kv != "bf16":
+        codes, scales = dd.quantize_kv_pages(pool, kv)
+        kv_pages = codes
+        kv_dtype = _lib.DTYPE_E4M3 if kv == "e4m3" else _lib.DTYPE_MXFP8
+        elem = 1.0
+        scale_bytes = D / 32 if kv == "mxfp8" else 0.0
+    else:
+        kv_pages = pool
+    cfg = dd.make_config(Hq, Hkv, D, tb.num_pages, kv_dtype=kv_dtype)
+    if heads:
+        lcfg = hs.shard_config(cfg, world)
+        kv_local = hs.shard_pages(kv_pages, rank, world)
+        sc_local = hs.shard_scales(scales, kv_dtype, rank, world, Hkv)
+        q_local = hs.shard_queries(q, cfg, rank, world)
+        del pool
+    else:
+        lcfg, kv_local, sc_local, q_local = cfg, kv_pages, scales, q
+    plan = dd.CascadePlan(lcfg, tb.indptr, tb.block_ids, tb.num_tokens)
+    plan.upload(dev)
+    info = plan.info()
+    ws = torch.empty(max(int(info.workspace_bytes), 256), dtype=torch.uint8, device=dev)
+    out_local = torch.empty_like(q_local)
+    lse = torch.empty(B, lcfg.num_qo_heads, dtype=torch.float32, device=dev)
+    out = torch.empty_like(q)
+    gathered = torch.empty((world,) + tuple(q_local.shape), dtype=q.dtype, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # > 126 MB L2
+    del q
+
+    def decode(plan_, q_in):
+        dd.cascade_decode(lcfg, plan_, q_in, kv_local, sc_local, out_local, lse, ws)
+        if heads:
+            if world > 1:
+                dist.all_gather_into_tensor(gathered, out_local)
+            else:
+                gathered[0].copy_(out_local)
+            dd.scatter_head_shards(cfg, world, gathered, out)
+            return out
+        return out_local
+
+    def step():
+        decode(plan, q_local)
+
+    ms_step, launches, clk = timed_steps(step, flush, args, world, rank, local, dev)
+    prof = profile_kernels(step, flush, min(args.steps, 20))
+    prof_steps = min(args.steps, 20)
+
     # Roofline of the dominant attention kernel: bytes (streaming kernels) or
-    # FLOPs (tcgen05 kernel) it is given by the plan, over its average launch.
+    # FLOPs (tcgen05 kernel) the plan gives it, over its average launch.
     kt = list(info.kv_tokens_by_kernel)
-    per_tok = 2 * Hkv * (D * elem + scale_bytes)
+    Hkv_l, Hq_l = lcfg.num_kv_heads, lcfg.num_qo_heads
+    per_tok = 2 * Hkv_l * (D * elem + scale_bytes)
     kernels = {}
     for idx, name in ((0, "attn_simple"), (1, "attn_mma")):
         if prof[name][1]:
             ms_l = prof[name][0] / prof[name][1]
-            byts = kt[idx] * per_tok + (B * Hq * D * 2 if idx == 1 or not kt[1] else 0)
+            byts = kt[idx] * per_tok + (B * Hq_l * D * 2 if idx == 1 or not kt[1] else 0)
             kernels[name] = {"bound": "hbm", "algorithmic": byts, "unit": "GB/s", "launch_ms": ms_l,
                              "achieved": byts / (ms_l * 1e-3) / 1e9, "peak": hbm_peak}
     if prof["attn_tc"][1]:
@@ -319,64 +450,56 @@ def run_ours(args):
         traffic = json.loads(tf.read_text()).get(f"{args.workload}:{attn_kind}")
 
     # End-to-end through the public API with host buffers: plan from the host
-    # block tables, H2D of the plan and the queries, decode, D2H of the output.
-    q_host = q.cpu().pin_memory()
-    out_host = torch.empty_like(q_host).pin_memory()
-    q_dev2 = torch.empty_like(q)
+    # block tables, H2D of the plan and the queries, decode (and, for the head
+    # split, the all-gather), D2H of the output.
+    q_host = q_local.cpu().pin_memory()
+    res = out if heads else out_local
+    out_host = torch.empty(res.shape, dtype=res.dtype).pin_memory()
+    q_dev2 = torch.empty_like(q_local)
 
     def e2e_step():
-        p2 = dd.CascadePlan(cfg, tb.indptr, tb.block_ids, tb.num_tokens)
+        p2 = dd.CascadePlan(lcfg, tb.indptr, tb.block_ids, tb.num_tokens)
         p2.device_buffer = plan.device_buffer
         p2.upload(dev)
         q_dev2.copy_(q_host, non_blocking=True)
-        dd.cascade_decode(cfg, p2, q_dev2, kv_pages, scales, out, lse, ws)
-        out_host.copy_(out, non_blocking=True)
+        r = decode(p2, q_dev2)
+        out_host.copy_(r, non_blocking=True)
         torch.cuda.synchronize()
         return p2.info().device_bytes
 
-    for _ in range(3):
-        e2e_step()
-    e2e_n = max(5, min(args.steps, 30))
-    if world > 1:
-        dist.barrier()
-    t0 = time.perf_counter()
-    plan_bytes = 0
-    for _ in range(e2e_n):
-        plan_bytes = e2e_step()
-    e2e_s = torch.tensor([(time.perf_counter() - t0) / e2e_n], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(e2e_s, op=dist.ReduceOp.MAX)
-    e2e_step_s = float(e2e_s.item())
+    e2e_step_s = e2e_time(e2e_step, args, world, dev)
+    plan_bytes = int(info.device_bytes)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         import oracle
 
-        pool_bits = pool.view(torch.int16).cpu().numpy().view(np.uint16)
-        if kv != "bf16":
-            cc = kv_pages.cpu().numpy()
-            ss = scales.cpu().numpy()
-            pool_bits = oracle.dequantize(cc, ss, kv)
-        qf = q.float().cpu().numpy()
+        pool_np = kv_pages.view(torch.int16).cpu().numpy().view(np.uint16) if kv == "bf16" else \
+            oracle.dequantize(kv_pages.cpu().numpy(), scales.cpu().numpy(), kv)
+        qf = q_local.float().cpu().numpy()
         threads = oracle_threads(tb)
-        rate, n, secs = cpu_sample_rate(tb, pool_bits, qf, args.cpu_budget, threads)
+        rate, n, secs = cpu_sample_rate(tb, pool_np, qf, args.cpu_budget, threads)
         cpu = {"value": rate, "unit": "queries/s", "cores": threads, "kind": "port",
                "sample": f"first {n} of {B} queries ({secs:.1f} s, {threads} threads)"}
 
     if rank == 0:
-        value = B * world / (ms_step * 1e-3)
+        kv_bytes = info.kv_tokens * per_tok + (2 * Hkv_l * 4 if kv == "e4m3" else 0)
+        eff_bytes = (kv_bytes + B * Hq_l * D * 4) * world  # every rank's share of the job
+        value = total_queries / (ms_step * 1e-3)
         gbs = eff_bytes / (ms_step * 1e-3) / 1e9
         line = {
             "metric": METRIC, "value": value, "unit": "queries/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "higher_is_better": True, "scaling": "weak" if w["split"] == "trees-per-rank" else "strong",
+            "vs_baseline": None,
             "dtype": "bf16" if kv == "bf16" else f"{kv} KV / bf16 compute", "data": "synthetic (seeded N(0,1))",
-            "config": {"workload": args.workload, "desc": WORKLOADS[args.workload]["desc"],
-                       "heads": [Hq, Hkv, D], "batch": B, "pages": tb.num_pages,
-                       "unique_kv_tokens": info.kv_tokens, "flat_kv_tokens": info.kv_tokens_flat,
-                       "plan_nodes": info.num_nodes, "l2": "flushed between steps (256 MiB write, untimed)",
-                       "parallelism": f"tree-partitioned x{world}"},
-            "effective_gbs": gbs, "hbm_frac": gbs / hbm_peak,
+            "config": {"workload": args.workload, "desc": w["desc"], "heads": [Hq, Hkv, D],
+                       "queries": total_queries, "pages_per_rank": tb.num_pages,
+                       "unique_kv_tokens_per_rank": info.kv_tokens,
+                       "flat_kv_tokens_per_rank": info.kv_tokens_flat, "plan_nodes": info.num_nodes,
+                       "l2": "flushed between steps (256 MiB write, untimed)",
+                       "parallelism": f"{w['split']} x{world}"},
+            "effective_gbs": gbs, "hbm_frac": gbs / (hbm_peak * world),
             "roofline": {"bound": dom["bound"], "kernel": attn_kind, "achieved": dom["achieved"],
                          "peak": dom["peak"], "unit": dom["unit"], "frac": dom["frac"],
                          "traffic": traffic, "peak_source": peak_kind + " (of measured)"
@@ -385,14 +508,97 @@ def run_ours(args):
             "kernel_rooflines": kernels,
             "kernel_ms_per_step": {k: v[0] / max(prof_steps, 1) for k, v in prof.items() if v[1]},
             "cpu_baseline": cpu,
-            "e2e": {"value": B * world / e2e_step_s, "unit": "queries/s",
-                    "h2d_bytes_per_step": int(q.numel() * 2 + plan_bytes),
-                    "d2h_bytes_per_step": int(out.numel() * 2), "ms_per_step": e2e_step_s * 1e3},
-            "clocks": clk, "gpu_launches": int(launches),
+            "e2e": {"value": total_queries / e2e_step_s, "unit": "queries/s",
+                    "h2d_bytes_per_step": int(q_local.numel() * 2 + plan_bytes),
+                    "d2h_bytes_per_step": int(res.numel() * 2), "ms_per_step": e2e_step_s * 1e3},
+            "clocks": clk, "gpu_launches": launches,
         }
         print(json.dumps(line), flush=True)
+
+
+def run_quant(args, world, rank, local, dev):
+    import torch
+
+    import dendrite_b200 as dd
+    from dendrite_b200 import _lib
+
+    fmt = WORKLOADS[args.workload]["fmt"]
+    hbm_peak, _, peak_kind = peaks()
+    bits = quant_pool_host(rank)
+    host = torch.from_numpy(bits.view(np.int16)).view(torch.bfloat16).pin_memory()
+    pool = host.to(dev)
+    codes, scales = dd.quantize_kv_pages(pool, fmt)
+    qws = torch.empty(1 << 20, dtype=torch.uint8, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def step():
+        dd.quantize_kv_pages(pool, fmt, codes=codes, scales=scales, workspace=qws)
+
+    ms_step, launches, clk = timed_steps(step, flush, args, world, rank, local, dev)
+    prof = profile_kernels(step, flush, min(args.steps, 20))
+    nbytes = quant_bytes(fmt)
+    qms = prof["quant"][0] / max(prof["quant"][1], 1)
+    codes_host = torch.empty(codes.shape, dtype=torch.uint8).pin_memory()
+    scales_host = torch.empty(scales.shape, dtype=scales.dtype).pin_memory()
+
+    def e2e_step():
+        pool.copy_(host, non_blocking=True)
+        step()
+        codes_host.copy_(codes, non_blocking=True)
+        scales_host.copy_(scales, non_blocking=True)
+        torch.cuda.synchronize()
+
+    e2e_s = e2e_time(e2e_step, args, world, dev)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        per, n = time_quant_cpu(bits, fmt, args.cpu_budget)
+        cpu = {"value": nbytes / per / 1e9, "unit": "GB/s", "cores": 1, "kind": "port",
+               "sample": f"the whole config-2 pool, {n} runs (single-threaded C oracle)"}
+    if rank == 0:
+        gbs = nbytes * world / (ms_step * 1e-3) / 1e9
+        traffic = None
+        tf = ROOT / "profiles" / "traffic.json"
+        if tf.exists():
+            traffic = json.loads(tf.read_text()).get(f"{args.workload}:quant")
+        line = {
+            "metric": QUANT_METRIC, "value": gbs, "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": f"bf16 -> {fmt}", "data": "synthetic (seeded N(0,1), 0.1% x50 outliers)",
+            "config": {"workload": args.workload, "desc": WORKLOADS[args.workload]["desc"],
+                       "algorithmic_bytes": nbytes, "l2": "flushed between steps (256 MiB write, untimed)"},
+            "roofline": {"bound": "hbm", "kernel": "quant", "achieved": nbytes / (qms * 1e-3) / 1e9,
+                         "peak": hbm_peak, "unit": "GB/s", "frac": nbytes / (qms * 1e-3) / 1e9 / hbm_peak,
+                         "traffic": traffic, "peak_source": peak_kind, "launch_ms": qms,
+                         "launches_per_step": prof["quant"][1] / max(min(args.steps, 20), 1)},
+            "cpu_baseline": cpu,
+            "e2e": {"value": nbytes * world / e2e_s / 1e9, "unit": "GB/s",
+                    "h2d_bytes_per_step": int(host.numel() * 2),
+                    "d2h_bytes_per_step": int(codes.numel() + scales.numel() * scales.element_size()),
+                    "ms_per_step": e2e_s * 1e3},
+            "clocks": clk, "gpu_launches": launches,
+        }
+        print(json.dumps(line), flush=True)
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    world, rank, local = dist_env()
     if world > 1:
-        dist.destroy_process_group()
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    try:
+        if WORKLOADS[args.workload]["kind"] == "quant":
+            run_quant(args, world, rank, local, dev)
+        else:
+            run_tree(args, world, rank, local, dev)
+    finally:
+        if world > 1:
+            dist.destroy_process_group()
 
 
 def main():

@@ -259,18 +259,24 @@ def quant_config(fmt: str, num_kv_heads: int, head_dim: int, src_dtype=torch.bfl
                        num_kv_heads, head_dim, PAGE_SIZE, scale_mode)
 
 
-def quantize_kv_pages(pages: torch.Tensor, fmt: str, scale_mode: int = 0, stream=None):
+def quantize_kv_pages(pages: torch.Tensor, fmt: str, scale_mode: int = 0, stream=None,
+                      codes: torch.Tensor | None = None, scales: torch.Tensor | None = None,
+                      workspace: torch.Tensor | None = None):
     """Quantise a page pool [P][2][Hkv][16][D] (bf16 or f32) to E4M3 codes +
-    per-head f32 scales ("e4m3") or E4M3 codes + E8M0 bytes ("mxfp8")."""
+    per-head f32 scales ("e4m3") or E4M3 codes + E8M0 bytes ("mxfp8").
+    codes / scales / workspace may be passed preallocated."""
     P, _, Hkv, _, D = pages.shape
     qc = quant_config(fmt, Hkv, D, pages.dtype, scale_mode)
-    codes = torch.empty(pages.shape, dtype=torch.uint8, device=pages.device)
-    if fmt == "e4m3":
-        scales = torch.empty(2, Hkv, dtype=torch.float32, device=pages.device)
-    else:
-        scales = torch.empty(P, 2, Hkv, PAGE_SIZE, D // 32, dtype=torch.uint8, device=pages.device)
-    ws = torch.empty(max(int(lib.dd_quantize_workspace_size(C.byref(qc))), 256), dtype=torch.uint8,
-                     device=pages.device)
+    if codes is None:
+        codes = torch.empty(pages.shape, dtype=torch.uint8, device=pages.device)
+    if scales is None:
+        if fmt == "e4m3":
+            scales = torch.empty(2, Hkv, dtype=torch.float32, device=pages.device)
+        else:
+            scales = torch.empty(P, 2, Hkv, PAGE_SIZE, D // 32, dtype=torch.uint8, device=pages.device)
+    need = max(int(lib.dd_quantize_workspace_size(C.byref(qc))), 256)
+    ws = workspace if workspace is not None and workspace.numel() >= need else \
+        torch.empty(need, dtype=torch.uint8, device=pages.device)
     check(lib.dd_quantize_kv_pages(C.byref(qc), _ptr(pages), P, _ptr(codes), _ptr(scales), _ptr(ws),
                                    ws.numel(), _stream(stream)), "dd_quantize_kv_pages")
     return codes, scales

@@ -263,7 +263,7 @@ static void build_items(dd_plan* p) {
     const int kind = kind_for(c, p->opts, rows);
     const int rt = row_tile_for(kind);
     p->kv_tokens_by_kind[kind] += n.num_tokens;
-    if (kind == kItemTc) p->tc_row_tokens += rows * n.num_tokens;
+    if (kind == kItemTc) p->tc_row_tokens += rows * n.num_tokens * Hkv;  // all KV heads
     const int64_t row_tiles = (rows + rt - 1) / rt;
     // Split-K chunking. Each extra chunk costs one more partial state per
     // (query, head) written and read back by the merge; allow at most 1/8 of

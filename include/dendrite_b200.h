@@ -136,8 +136,8 @@ typedef struct dd_plan_info {
   /* Unique KV tokens read by each attention kernel: [0] CUDA-core kernel,
    * [1] streaming tensor-core (mma) kernel, [2] tcgen05 kernel (wide nodes). */
   int64_t kv_tokens_by_kernel[3];
-  /* Sum over tcgen05 nodes of (query rows x tokens): the kernel's
-   * 4 * head_dim FLOPs per unit (Q.K^T and P.V). */
+  /* Sum over tcgen05 nodes and KV heads of (query rows x tokens): the
+   * kernel's 4 * head_dim FLOPs per unit (Q.K^T and P.V). */
   int64_t tc_row_tokens;
 } dd_plan_info;
 
