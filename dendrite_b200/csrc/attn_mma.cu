@@ -151,170 +151,191 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
 
   if (warp >= kStreams) {
     // ------------------------------------------------------------ producer
-    // Producer warp kStreams + c drives stream c from its lane 0, so a stall
-    // on one stream's reads never delays another stream.
+    // Producer warp kStreams + c drives stream c with all 32 lanes, so a
+    // stall on one stream's reads never delays another stream. Lane l holds
+    // the id of page chunk_base + l of the current item (and of the next
+    // 32-page chunk), read 32 at a time one chunk ahead, so a stage issues no
+    // dependent global read; lanes issue the stage's copies in parallel.
     const int c = warp - kStreams;
-    if (lane == 0) {
-      StreamShared& sh = ss[c];
-      uint8_t* base = smem + c * C::kStreamBytes;
-      uint8_t* qbuf = base + S * C::kStageAll + C::kConvBytes;
-      int stage_idx = 0, item_count = 0;
-      bool need_item = true, finished = false;
-      WorkItem it{};
-      const uint32_t* pages = nullptr;
-      int pi = 0;                      // next page of the item
-      uint32_t nxt0 = 0, nxt1 = 0;     // prefetched ids of pages pi, pi+1
-      // The next item is prefetched one dependent read per stage (claim the
-      // index, read the item, read its first page ids), so the latency chain
-      // overlaps the current item's stages instead of stalling the stream.
-      int pf_state = 0, pf_idx = 0;
-      WorkItem pf_it{};
-      const uint32_t* pf_pages = nullptr;
-      uint32_t pf0 = 0, pf1 = 0;
-      auto pf_step = [&]() {
-        if (pf_state == 0) {
-          pf_idx = (int)atomicAdd(&a.err->work_counter, 1u);
-        } else if (pf_state == 1) {
-          if (pf_idx < a.num_items) pf_it = resolve_item_idx(a, pf_idx, pf_pages, kMmaRows);
-        } else if (pf_state == 2) {
-          if (pf_idx < a.num_items) {
-            pf0 = pf_it.npages > 0 ? pf_pages[0] : 0u;
-            pf1 = pf_it.npages > 1 ? pf_pages[1] : 0u;
+    StreamShared& sh = ss[c];
+    uint8_t* base = smem + c * C::kStreamBytes;
+    uint8_t* qbuf = base + S * C::kStageAll + C::kConvBytes;
+    int stage_idx = 0, item_count = 0;
+    bool need_item = true, finished = false;
+    WorkItem it{};
+    const uint32_t* pages = nullptr;
+    int pi = 0;                        // next page of the item
+    int chunk_base = 0;                // first page of the chunk in cur_id
+    uint32_t cur_id = 0, nxt_id = 0;   // lane l: ids of pages chunk_base + l, + 32
+    // The next item is prefetched one dependent read per stage (claim the
+    // index, read the item, read its first 64 page ids), so the latency chain
+    // overlaps the current item's stages instead of stalling the stream.
+    int pf_state = 0, pf_idx = 0;
+    WorkItem pf_it{};
+    const uint32_t* pf_pages = nullptr;
+    uint32_t pf_id = 0, pf_id2 = 0;
+    auto pf_step = [&]() {
+      if (pf_state == 0) {
+        uint32_t v = 0;
+        if (lane == 0) v = atomicAdd(&a.err->work_counter, 1u);
+        pf_idx = (int)__shfl_sync(0xffffffffu, v, 0);
+      } else if (pf_state == 1) {
+        if (pf_idx < a.num_items) pf_it = resolve_item_idx(a, pf_idx, pf_pages, kMmaRows);
+      } else if (pf_state == 2) {
+        if (pf_idx < a.num_items) {
+          pf_id = lane < pf_it.npages ? pf_pages[lane] : 0u;
+          pf_id2 = lane + 32 < pf_it.npages ? pf_pages[lane + 32] : 0u;
+        }
+      }
+      ++pf_state;
+    };
+    long long t_pf = 0, t_empty = 0, t_qe = 0;
+    DD_TSTART(tlife)
+    uint64_t t_idle = global_ns();
+    while (!finished) {
+      if (abort_flag) break;
+      bool done = false;
+      if (need_item) {
+        DD_TSTART(tpf)
+        while (pf_state < 3) pf_step();  // completes the prefetch (or does it all when disabled)
+        DD_TACC(t_pf, tpf)
+        done = pf_idx >= a.num_items;
+        if (!done) {
+          it = pf_it;
+          pages = pf_pages;
+          pi = 0;
+          chunk_base = 0;
+          cur_id = pf_id;
+          nxt_id = pf_id2;
+        }
+        pf_state = 0;
+      }
+      // Wait (bounded, non-blocking poll) for a free stage.
+      const int s = stage_idx % S;
+      if (stage_idx >= S) {
+        DD_TSTART(tem)
+        bool ok = true;
+        while (!mbar_try_wait(&sh.empty[s], ((stage_idx / S) - 1) & 1)) {
+          if (global_ns() - t_idle > kWaitLimitNs) {
+            ok = false;
+            break;
           }
         }
-        ++pf_state;
-      };
-      long long t_pf = 0, t_empty = 0, t_qe = 0;
-      DD_TSTART(tlife)
-      uint64_t t_idle = global_ns();
-      while (!finished) {
-        if (abort_flag) break;
-        bool done = false;
-        if (need_item) {
-          DD_TSTART(tpf)
-          while (pf_state < 3) pf_step();  // completes the prefetch (or does it all when disabled)
-          DD_TACC(t_pf, tpf)
-          done = pf_idx >= a.num_items;
-          if (!done) {
-            it = pf_it;
-            pages = pf_pages;
-            pi = 0;
-            nxt0 = pf0;
-            nxt1 = pf1;
+        DD_TACC(t_empty, tem)
+        if (!__all_sync(0xffffffffu, ok)) {
+          if (lane == 0) {
+            abort_flag = 1;
+            report_error(a.err, kDevErrWaitTimeout, 1);
           }
-          pf_state = 0;
-        }
-        // Wait (bounded, non-blocking poll) for a free stage.
-        const int s = stage_idx % S;
-        if (stage_idx >= S) {
-          DD_TSTART(tem)
-          while (!mbar_try_wait(&sh.empty[s], ((stage_idx / S) - 1) & 1)) {
-            if (global_ns() - t_idle > kWaitLimitNs) {
-              abort_flag = 1;
-              report_error(a.err, kDevErrWaitTimeout, 1);
-              break;
-            }
-          }
-          DD_TACC(t_empty, tem)
-          if (abort_flag) break;
-        }
-        // The Q buffer of the stream is reused once the consumer has read it.
-        DD_TSTART(tqe)
-        if (need_item && !done && item_count >= 1 &&
-            !mbar_wait(&sh.q_empty, (item_count - 1) & 1, &abort_flag, a.err))
           break;
-        DD_TACC(t_qe, tqe)
-        StageMeta m;
-        uint32_t bytes = 0;
-        if (done) {
+        }
+      }
+      // The Q buffer of the stream is reused once the consumer has read it.
+      DD_TSTART(tqe)
+      if (need_item && !done && item_count >= 1 &&
+          !__all_sync(0xffffffffu, mbar_wait(&sh.q_empty, (item_count - 1) & 1, &abort_flag, a.err)))
+        break;
+      DD_TACC(t_qe, tqe)
+      if (done) {
+        if (lane == 0) {
+          StageMeta m;
           m.item_slot = 0;
           m.flags = kDone;
           m.np = 0;
           m.invalid = 0;
           m.page0 = 0;
-          finished = true;
-        } else {
-          const int k = item_count & 1;
+          sh.meta[s] = m;
+          mbar_arrive_expect_tx(&sh.full[s], 0);
+        }
+        finished = true;
+      } else {
+        const int k = item_count & 1;
+        const int np = min(kStepPages, it.npages - pi);
+        // Ids of this stage's pages j < np from the lanes' chunk registers.
+        uint32_t pg[kStepPages];
+#pragma unroll
+        for (int j = 0; j < kStepPages; ++j) {
+          const int p = pi + j - chunk_base;  // 0..32
+          const uint32_t x = __shfl_sync(0xffffffffu, cur_id, p & 31);
+          const uint32_t y = __shfl_sync(0xffffffffu, nxt_id, p & 31);
+          pg[j] = p < 32 ? x : y;
+        }
+        int invalid = 0;
+#pragma unroll
+        for (int j = 0; j < kStepPages; ++j)
+          if (j < np && pg[j] >= (uint32_t)a.num_pages) {
+            if (lane == 0) report_error(a.err, kDevErrBadPage, pg[j]);
+            invalid |= 1 << j;
+            pg[j] = 0;  // load something harmless; the consumer skips the page
+          }
+        const uint32_t qbytes = need_item ? (uint32_t)it.nrows * D * 2 : 0u;
+        const uint32_t bytes = (uint32_t)np * 2 * (C::kSliceRaw + C::kMxBytes) + qbytes;
+        if (lane == 0) {
           if (need_item) sh.items[k] = it;
-          const int np = min(kStepPages, it.npages - pi);
-          uint32_t pg[2] = {nxt0, nxt1};
-          int invalid = 0;
-          for (int j = 0; j < np; ++j)
-            if (pg[j] >= (uint32_t)a.num_pages) {
-              report_error(a.err, kDevErrBadPage, pg[j]);
-              invalid |= 1 << j;
-              pg[j] = 0;  // load something harmless; the consumer skips the page
-            }
+          StageMeta m;
           m.item_slot = (int8_t)k;
           m.flags = (int8_t)((need_item ? kFirst : 0) | (pi + np >= it.npages ? kLast : 0));
           m.np = (int8_t)np;
           m.invalid = (int8_t)invalid;
           m.page0 = pi;
           sh.meta[s] = m;
-          const uint32_t qbytes = need_item ? (uint32_t)it.nrows * D * 2 : 0u;
-          bytes = (uint32_t)np * 2 * (C::kSliceRaw + C::kMxBytes) + qbytes;
           mbar_arrive_expect_tx(&sh.full[s], bytes);
-          if (qbytes) {
-            // Read every row's query index first (independent loads), then
-            // issue the row copies.
-            const uint16_t* qsrc[kMmaRows];
-#pragma unroll
-            for (int r = 0; r < kMmaRows; ++r) {
-              qsrc[r] = nullptr;
-              if (r < it.nrows) {
-                const int rr = it.row0 + r, qi = rr / a.g;
-                const int hq = qo_head_of(a.gqa_map, it.kv_head, rr % a.g, a.Hkv, a.g);
-                const int qid = a.qorder ? a.qorder[it.q_begin + qi] : it.q_begin + qi;
-                qsrc[r] = reinterpret_cast<const uint16_t*>(a.q) + ((size_t)qid * a.Hq + hq) * D;
-              }
-            }
-#pragma unroll
-            for (int r = 0; r < kMmaRows; ++r)
-              if (r < it.nrows) bulk_load(qbuf + r * C::kQRowBytes, qsrc[r], D * 2, &sh.full[s]);
-          }
+        }
+        __syncwarp();
+        // Lane r < nrows copies query row r; lane 16 + 2j + kv copies page
+        // j's K (kv = 0) or V slice.
+        if (qbytes && lane < it.nrows) {
+          const int rr = it.row0 + lane, qi = rr / a.g;
+          const int hq = qo_head_of(a.gqa_map, it.kv_head, rr % a.g, a.Hkv, a.g);
+          const int qid = a.qorder ? a.qorder[it.q_begin + qi] : it.q_begin + qi;
+          bulk_load(qbuf + lane * C::kQRowBytes,
+                    reinterpret_cast<const uint16_t*>(a.q) + ((size_t)qid * a.Hq + hq) * D, D * 2,
+                    &sh.full[s]);
+        }
+        const int l2 = lane - 16;
+        if (l2 >= 0 && l2 < 2 * np) {
+          const int j = l2 >> 1, kv = l2 & 1;
+          const uint32_t pid = j == 0 ? pg[0] : pg[1];
+          const int y = (int)((((int64_t)pid * 2 + kv) * a.Hkv + it.kv_head) * kPageSize);
           uint8_t* st = base + s * C::kStageAll;
-          for (int j = 0; j < np; ++j)
-            for (int kv = 0; kv < 2; ++kv) {
-              const int y = (int)((((int64_t)pg[j] * 2 + kv) * a.Hkv + it.kv_head) * kPageSize);
-              uint8_t* dst = st + (kv * kStepPages + j) * C::kSliceRaw;
-              if (KV == kKvBf16 && D == 128)
-                tma_load_3d(dst, &kv_map, 0, y, 0, &sh.full[s]);
-              else
-                tma_load_2d(dst, &kv_map, 0, y, &sh.full[s]);
-              if (KV == kKvMx)
-                bulk_load(st + C::kRawStage + (kv * kStepPages + j) * C::kMxBytes,
-                          reinterpret_cast<const uint8_t*>(a.scales) + (size_t)y * (D / 32),
-                          C::kMxBytes, &sh.full[s]);
-            }
-          pi += np;
-          // Prefetch the next stage's page ids now; they are needed only after
-          // the next free-stage wait.
-          nxt0 = pi < it.npages ? pages[pi] : 0u;
-          nxt1 = pi + 1 < it.npages ? pages[pi + 1] : 0u;
-          if (need_item) need_item = false;
-          if (pi >= it.npages) {
-            need_item = true;
-            ++item_count;
-          }
+          uint8_t* dst = st + (kv * kStepPages + j) * C::kSliceRaw;
+          if (KV == kKvBf16 && D == 128)
+            tma_load_3d(dst, &kv_map, 0, y, 0, &sh.full[s]);
+          else
+            tma_load_2d(dst, &kv_map, 0, y, &sh.full[s]);
+          if (KV == kKvMx)
+            bulk_load(st + C::kRawStage + (kv * kStepPages + j) * C::kMxBytes,
+                      reinterpret_cast<const uint8_t*>(a.scales) + (size_t)y * (D / 32),
+                      C::kMxBytes, &sh.full[s]);
         }
-        if (done) {
-          sh.meta[s] = m;
-          mbar_arrive_expect_tx(&sh.full[s], 0);
+        pi += np;
+        if (pi - chunk_base >= 32) {
+          // Entering the next chunk: its ids are in nxt_id; read the one after.
+          chunk_base += 32;
+          cur_id = nxt_id;
+          nxt_id = chunk_base + 32 + lane < it.npages ? pages[chunk_base + 32 + lane] : 0u;
         }
-        ++stage_idx;
-        t_idle = global_ns();
-#ifndef DD_EXPERIMENT_NO_PREFETCH
-        if (!finished && pf_state < 3) pf_step();
-#endif
+        if (need_item) need_item = false;
+        if (pi >= it.npages) {
+          need_item = true;
+          ++item_count;
+        }
       }
-      long long t_life = 0;
-      DD_TACC(t_life, tlife)
+      ++stage_idx;
+      t_idle = global_ns();
+#ifndef DD_EXPERIMENT_NO_PREFETCH
+      if (!finished && pf_state < 3) pf_step();
+#endif
+    }
+    long long t_life = 0;
+    DD_TACC(t_life, tlife)
+    if (lane == 0) {
       DD_TFLUSH(a, 2, t_empty)
       DD_TFLUSH(a, 3, t_life)
       DD_TFLUSH(a, 4, t_qe)
       DD_TFLUSH(a, 5, t_pf)
-      (void)t_pf; (void)t_empty; (void)t_qe; (void)t_life;
     }
+    (void)t_pf; (void)t_empty; (void)t_qe; (void)t_life;
   } else {
     // ------------------------------------------------------------ consumer
     StreamShared& sh = ss[warp];

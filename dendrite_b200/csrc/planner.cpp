@@ -77,7 +77,11 @@ namespace dd {
 static int kind_for(const dd_attn_config& c, const dd_plan_options& o, int64_t rows) {
   if (c.kv_dtype == DD_DTYPE_F32 || c.q_dtype != DD_DTYPE_BF16 || c.head_dim > 128)
     return kItemSimple;
+#ifdef DD_EXPERIMENT_TC_MIN_ROWS
+  if (o.use_tensor_cores && rows >= DD_EXPERIMENT_TC_MIN_ROWS && c.head_dim == 128 && c.kv_dtype != DD_DTYPE_F32 &&
+#else
   if (o.use_tensor_cores && rows >= 128 && c.head_dim == 128 && c.kv_dtype != DD_DTYPE_F32 &&
+#endif
       dd_tc_available())
     return kItemTc;
   return kItemMma;
