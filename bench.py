@@ -419,8 +419,8 @@ def run_tree(args, world, rank, local, dev):
         decode(plan, q_local)
 
     ms_step, launches, clk = timed_steps(step, flush, args, world, rank, local, dev)
-    prof = profile_kernels(step, flush, min(args.steps, 20))
     prof_steps = min(args.steps, 20)
+    prof = profile_kernels(step, flush, prof_steps)
 
     # Roofline of the dominant attention kernel: bytes (streaming kernels) or
     # FLOPs (tcgen05 kernel) the plan gives it, over its average launch.
@@ -428,21 +428,23 @@ def run_tree(args, world, rank, local, dev):
     Hkv_l, Hq_l = lcfg.num_kv_heads, lcfg.num_qo_heads
     per_tok = 2 * Hkv_l * (D * elem + scale_bytes)
     kernels = {}
+    # Times are per step (a family may launch more than once per step: the
+    # tcgen05 family is one launch per CTA size).
     for idx, name in ((0, "attn_simple"), (1, "attn_mma")):
         if prof[name][1]:
-            ms_l = prof[name][0] / prof[name][1]
+            ms_l = prof[name][0] / prof_steps
             byts = kt[idx] * per_tok + (B * Hq_l * D * 2 if idx == 1 or not kt[1] else 0)
             kernels[name] = {"bound": "hbm", "algorithmic": byts, "unit": "GB/s", "launch_ms": ms_l,
                              "achieved": byts / (ms_l * 1e-3) / 1e9, "peak": hbm_peak}
     if prof["attn_tc"][1]:
-        ms_l = prof["attn_tc"][0] / prof["attn_tc"][1]
+        ms_l = prof["attn_tc"][0] / prof_steps
         flops = 4.0 * D * info.tc_row_tokens
         kernels["attn_tc"] = {"bound": "tensor", "algorithmic": flops, "unit": "TFLOP/s",
                               "launch_ms": ms_l, "achieved": flops / (ms_l * 1e-3) / 1e12,
                               "peak": tc_peak}
     for k in kernels.values():
         k["frac"] = k["achieved"] / k["peak"]
-    attn_kind = max(kernels, key=lambda k: kernels[k]["launch_ms"] * prof[k][1])
+    attn_kind = max(kernels, key=lambda k: kernels[k]["launch_ms"])
     dom = kernels[attn_kind]
     traffic = None
     tf = ROOT / "profiles" / "traffic.json"

@@ -12,6 +12,7 @@ cudaError_t launch_attn_simple(const AttnArgs& a, dim3 grid, cudaStream_t st);
 int launch_attn_mma(const AttnArgs& a, int64_t num_pages, cudaStream_t st);
 bool mma_supported(int D, int kv_dtype);
 int launch_attn_tc(const AttnArgs& a, int64_t num_pages, int num_items, cudaStream_t st);
+int launch_attn_tc2(const AttnArgs& a, int64_t num_pages, int num_items, cudaStream_t st);
 cudaError_t launch_merge(const MergeArgs& a, cudaStream_t st);
 
 static int cuda_fail(cudaError_t e, const char* what) {
@@ -137,7 +138,8 @@ extern "C" int dd_cascade_decode(const dd_attn_config* cfg, const dd_plan* p, co
   // nodes, HBM-bound); the merge waits for both. The fork/join is a pair of
   // events, so it also captures into a CUDA graph.
   const int n_tc = (int)p->items[kItemTc].size();
-  const bool fork = n_tc > 0 && !prof_timing_on() &&
+  const int n_tc2 = (int)p->items[kItemTc2].size();
+  const bool fork = n_tc + n_tc2 > 0 && !prof_timing_on() &&
                     (!p->items[kItemMma].empty() || !p->items[kItemSimple].empty());
   SideStream* side = nullptr;
   if (fork) {
@@ -147,6 +149,11 @@ extern "C" int dd_cascade_decode(const dd_attn_config* cfg, const dd_plan* p, co
     if (e == cudaSuccess) e = cudaStreamWaitEvent(side->stream, side->fork, 0);
     if (e != cudaSuccess) return cuda_fail(e, "side stream fork");
   }
+  if (n_tc2) {
+    a.items = reinterpret_cast<const WorkItem*>(base + p->off_items[kItemTc2]);
+    rc = launch_attn_tc2(a, cfg->num_pages, n_tc2, fork ? side->stream : st);
+    if (rc) return rc;
+  }
   if (n_tc) {
     a.items = reinterpret_cast<const WorkItem*>(base + p->off_items[kItemTc]);
     rc = launch_attn_tc(a, cfg->num_pages, n_tc, fork ? side->stream : st);
@@ -154,7 +161,7 @@ extern "C" int dd_cascade_decode(const dd_attn_config* cfg, const dd_plan* p, co
   }
   for (int k = 0; k < kNumItemKinds; ++k) {
     const int n = (int)p->items[k].size();
-    if (!n || k == kItemTc) continue;
+    if (!n || k == kItemTc || k == kItemTc2) continue;
     a.items = reinterpret_cast<const WorkItem*>(base + p->off_items[k]);
     if (k == kItemSimple) {
       e = launch_attn_simple(a, dim3(n), st);

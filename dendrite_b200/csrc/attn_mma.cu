@@ -167,24 +167,33 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
     int pi = 0;                        // next page of the item
     int chunk_base = 0;                // first page of the chunk in cur_id
     uint32_t cur_id = 0, nxt_id = 0;   // lane l: ids of pages chunk_base + l, + 32
+    int qid = 0;                       // lane r < nrows: query of the item's row r
     // The next item is prefetched one dependent read per stage (claim the
-    // index, read the item, read its first 64 page ids), so the latency chain
-    // overlaps the current item's stages instead of stalling the stream.
+    // index, read the item, read its first 64 page ids and its rows' query
+    // indices), and no step uses a value read in the same step, so the
+    // latency chain overlaps the current item's stages.
+    constexpr int kPfStates = 4;
     int pf_state = 0, pf_idx = 0;
+    uint32_t pf_claim = 0;             // lane 0: claimed item index, in flight
     WorkItem pf_it{};
     const uint32_t* pf_pages = nullptr;
     uint32_t pf_id = 0, pf_id2 = 0;
+    int pf_qid = 0;                    // lane r < nrows: query index of row r
     auto pf_step = [&]() {
       if (pf_state == 0) {
-        uint32_t v = 0;
-        if (lane == 0) v = atomicAdd(&a.err->work_counter, 1u);
-        pf_idx = (int)__shfl_sync(0xffffffffu, v, 0);
+        if (lane == 0) pf_claim = atomicAdd(&a.err->work_counter, 1u);
       } else if (pf_state == 1) {
+        pf_idx = (int)__shfl_sync(0xffffffffu, pf_claim, 0);
         if (pf_idx < a.num_items) pf_it = resolve_item_idx(a, pf_idx, pf_pages, kMmaRows);
       } else if (pf_state == 2) {
         if (pf_idx < a.num_items) {
           pf_id = lane < pf_it.npages ? pf_pages[lane] : 0u;
           pf_id2 = lane + 32 < pf_it.npages ? pf_pages[lane + 32] : 0u;
+        }
+      } else if (pf_state == 3) {
+        if (pf_idx < a.num_items && lane < pf_it.nrows) {
+          const int qi = (pf_it.row0 + lane) / a.g;
+          pf_qid = a.qorder ? a.qorder[pf_it.q_begin + qi] : pf_it.q_begin + qi;
         }
       }
       ++pf_state;
@@ -197,7 +206,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
       bool done = false;
       if (need_item) {
         DD_TSTART(tpf)
-        while (pf_state < 3) pf_step();  // completes the prefetch (or does it all when disabled)
+        while (pf_state < kPfStates) pf_step();  // completes the prefetch (or all of it when disabled)
         DD_TACC(t_pf, tpf)
         done = pf_idx >= a.num_items;
         if (!done) {
@@ -207,6 +216,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
           chunk_base = 0;
           cur_id = pf_id;
           nxt_id = pf_id2;
+          qid = pf_qid;
         }
         pf_state = 0;
       }
@@ -285,9 +295,8 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
         // Lane r < nrows copies query row r; lane 16 + 2j + kv copies page
         // j's K (kv = 0) or V slice.
         if (qbytes && lane < it.nrows) {
-          const int rr = it.row0 + lane, qi = rr / a.g;
+          const int rr = it.row0 + lane;
           const int hq = qo_head_of(a.gqa_map, it.kv_head, rr % a.g, a.Hkv, a.g);
-          const int qid = a.qorder ? a.qorder[it.q_begin + qi] : it.q_begin + qi;
           bulk_load(qbuf + lane * C::kQRowBytes,
                     reinterpret_cast<const uint16_t*>(a.q) + ((size_t)qid * a.Hq + hq) * D, D * 2,
                     &sh.full[s]);
@@ -324,7 +333,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
       ++stage_idx;
       t_idle = global_ns();
 #ifndef DD_EXPERIMENT_NO_PREFETCH
-      if (!finished && pf_state < 3) pf_step();
+      if (!finished && pf_state < kPfStates) pf_step();
 #endif
     }
     long long t_life = 0;

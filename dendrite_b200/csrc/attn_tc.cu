@@ -37,16 +37,11 @@
 // (crates/dendrite-core/src/attention/backend.rs:254-262) over the node's
 // tokens; the normalised partial state goes to the workspace and is merged
 // along each query's path by merge.cu.
-#include "dd_device.cuh"
+#include "tc_common.cuh"
 
 namespace dd {
 
 constexpr int kTcRows = 256;            // rows per item: two sub-tiles of 128
-constexpr int kTcTok = 128;             // tokens per tile
-constexpr int kTcPagesPerTile = kTcTok / kPageSize;
-constexpr int kTcSlotBytes = kTcTok * 128 * 2;   // 128 tokens x 128 dims bf16
-constexpr int kTcHalfBytes = kTcTok * 128;       // one 64-dim half of a slot
-constexpr int kTcQBytes = 128 * 128 * 2;         // one 128-row Q sub-tile
 constexpr int kTcStages = 3;                     // FP8 staging ring (K or V tile each)
 constexpr int kTcStageCodes = kTcTok * 128;      // 128 tokens x 128 E4M3 codes
 constexpr int kTcStageExps = kTcPagesPerTile * 64;  // MXFP8 exponents of a staged tile
@@ -61,95 +56,16 @@ constexpr int kTcStageBytes = kTcStageCodes + kTcStageExps;
 template <int KV>
 struct TcCfg {
   static constexpr bool kFp8 = KV != DD_DTYPE_BF16;
+#ifdef DD_EXPERIMENT_TC_SLOTS
+  static constexpr int kSlots = kFp8 ? 3 : DD_EXPERIMENT_TC_SLOTS;
+#else
   static constexpr int kSlots = kFp8 ? 3 : 4;    // K/V ring slots (32 KiB each)
+#endif
   static constexpr int kThreads = kFp8 ? 384 : 320;
   static constexpr int kSmem =
       2 * kTcQBytes + kSlots * kTcSlotBytes + (kFp8 ? kTcStages * kTcStageBytes : 0) + 1024;
 };
-constexpr int kTcMaxSlots = 4;
-constexpr uint32_t kTmemCols = 512;
-// Per sub-tile x: S (then P over it) at col_s(x), O at col_o(x).
-__device__ __forceinline__ uint32_t col_s(int x) { return (uint32_t)x * 256u; }
-__device__ __forceinline__ uint32_t col_o(int x) { return (uint32_t)x * 256u + 128u; }
-constexpr float kRescaleThreshold = 8.0f;  // log2 units
-
-// Instruction descriptors, kind::f16, D f32, A/B bf16, M = 128, N = 128.
-constexpr uint32_t kIdescQK = (1u << 4) | (1u << 7) | (1u << 10) | ((128u >> 3) << 17) |
-                              ((128u >> 4) << 24);
-constexpr uint32_t kIdescPV = kIdescQK | (1u << 16);  // B (V) is MN-major
-
-// Shared-memory matrix descriptor, 128-byte swizzle, sm_100 version bits.
-__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
-  uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);
-  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
-  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
-  d |= (uint64_t)1 << 46;
-  d |= (uint64_t)2 << 61;
-  return d;
-}
-
-__device__ __forceinline__ void umma_ss(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
-                                        uint32_t acc) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
-      "l"(a), "l"(b), "r"(idesc), "r"(acc));
-}
-__device__ __forceinline__ void umma_ts(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t idesc,
-                                        uint32_t acc) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d),
-      "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc));
-}
-__device__ __forceinline__ void umma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                   smem_u32(bar))
-               : "memory");
-}
-__device__ __forceinline__ void tc_fence_before() {
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void tc_fence_after() {
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
-
-// 32 lanes x 32 columns of 32-bit: thread i gets columns [col, col+32) of lane i.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
-  uint32_t r[32];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
-      "%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]),
-        "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]),
-        "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-}
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
-      "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
-      "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7]),
-      "f"(v[8]), "f"(v[9]), "f"(v[10]), "f"(v[11]), "f"(v[12]), "f"(v[13]), "f"(v[14]), "f"(v[15]),
-      "f"(v[16]), "f"(v[17]), "f"(v[18]), "f"(v[19]), "f"(v[20]), "f"(v[21]), "f"(v[22]), "f"(v[23]),
-      "f"(v[24]), "f"(v[25]), "f"(v[26]), "f"(v[27]), "f"(v[28]), "f"(v[29]), "f"(v[30]), "f"(v[31])
-      : "memory");
-}
-__device__ __forceinline__ void tmem_st16u(uint32_t taddr, const uint32_t (&v)[16]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
-      "%14,%15,%16};" ::"r"(taddr),
-      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
-      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
-      : "memory");
-}
-
+constexpr int kTcMaxSlots = 5;
 // Wait-time and phase counters for pipeline experiments (compiled in only
 // with DD_EXPERIMENT_TIMING; summed into the workspace header's pad words).
 #ifdef DD_EXPERIMENT_TIMING
@@ -176,49 +92,6 @@ struct TcBars {
   int abort;
 };
 
-// 32 columns of this thread's TMEM lane, times f, written back.
-__device__ __forceinline__ void tmem_scale32(uint32_t taddr, float f) {
-  float o[32];
-  tmem_ld32(taddr, o);
-  tmem_wait_ld();
-#pragma unroll
-  for (int i = 0; i < 32; i += 2) {
-    const uint64_t v = f2_fma(f2_pack(o[i], o[i + 1]), f2_pack(f, f), 0ull);
-    o[i] = f2_lo(v);
-    o[i + 1] = f2_hi(v);
-  }
-  tmem_st32(taddr, o);
-}
-
-// Softmax of one 64-token chunk (s[], scores already masked): P = exp2(s *
-// scale - m), accumulated into *acc, written as bf16 hi / lo terms into the
-// chunk's own TMEM columns (hi: +0..31, lo: +32..63), which held its scores.
-__device__ __forceinline__ void softmax_chunk(float (&s)[64], uint64_t sc2, uint64_t nm2,
-                                              uint64_t& acc, uint32_t taddr) {
-  uint64_t a0 = 0ull, a1 = 0ull;
-#pragma unroll
-  for (int i = 0; i < 64; i += 4) {
-    const uint64_t x0 = f2_fma(f2_pack(s[i], s[i + 1]), sc2, nm2);
-    const uint64_t x1 = f2_fma(f2_pack(s[i + 2], s[i + 3]), sc2, nm2);
-    s[i] = fast_exp2(f2_lo(x0));
-    s[i + 1] = fast_exp2(f2_hi(x0));
-    s[i + 2] = fast_exp2(f2_lo(x1));
-    s[i + 3] = fast_exp2(f2_hi(x1));
-    a0 = f2_add(a0, f2_pack(s[i], s[i + 1]));
-    a1 = f2_add(a1, f2_pack(s[i + 2], s[i + 3]));
-  }
-  acc = f2_add(acc, f2_add(a0, a1));
-#pragma unroll
-  for (int c = 0; c < 2; ++c) {
-    uint32_t hi[16], lo[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i)
-      split_bf16x2_packed(f2_pack(s[c * 32 + 2 * i], s[c * 32 + 2 * i + 1]), hi[i], lo[i]);
-    tmem_st16u(taddr + c * 16, hi);
-    tmem_st16u(taddr + 32 + c * 16, lo);
-  }
-}
-
 template <int KV>
 __global__ void __launch_bounds__(TcCfg<KV>::kThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap kv_map, AttnArgs a) {
@@ -241,6 +114,7 @@ __global__ void __launch_bounds__(TcCfg<KV>::kThreads, 1)
 #ifdef DD_EXPERIMENT_TIMING
   long long tacc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
   long long tacc2[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  const long long t_entry = clock64();
 #endif
 
   if (threadIdx.x == 0) {
@@ -273,6 +147,9 @@ __global__ void __launch_bounds__(TcCfg<KV>::kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = bars.tmem_base;
+#ifdef DD_EXPERIMENT_TIMING
+  if (threadIdx.x == 64) tacc2[5] += clock64() - t_entry;  // setup: barriers, TMEM alloc
+#endif
   volatile int* abort = &bars.abort;
 
   if (warp == 0) {
@@ -484,6 +361,9 @@ __global__ void __launch_bounds__(TcCfg<KV>::kThreads, 1)
       }
       fence_proxy_async_smem();
       mbar_arrive(&bars.q_ready);
+#ifdef DD_EXPERIMENT_TIMING
+      if (threadIdx.x == 64) tacc2[6] += clock64() - t_entry;  // Q copied
+#endif
     }
     const bool active = x == 0 || has_b;
     const float scale_log2 = a.scale_log2;
@@ -576,6 +456,9 @@ __global__ void __launch_bounds__(TcCfg<KV>::kThreads, 1)
       mbar_arrive(&bars.p_full[x]);
       TCP_MARK(4, tp)
     }
+#ifdef DD_EXPERIMENT_TIMING
+    if (threadIdx.x == 64) tacc2[7] += clock64() - t_entry;  // all tiles done
+#endif
     // Epilogue: the normalised O row and its LSE.
     if (active) {
       const float L = f2_lo(lsum) + f2_hi(lsum);

@@ -77,17 +77,19 @@ namespace dd {
 static int kind_for(const dd_attn_config& c, const dd_plan_options& o, int64_t rows) {
   if (c.kv_dtype == DD_DTYPE_F32 || c.q_dtype != DD_DTYPE_BF16 || c.head_dim > 128)
     return kItemSimple;
+  const bool tc = o.use_tensor_cores && c.head_dim == 128 && dd_tc_available();
+  if (tc && o.cta_pairs && rows > 256 && c.kv_dtype == DD_DTYPE_BF16) return kItemTc2;
 #ifdef DD_EXPERIMENT_TC_MIN_ROWS
-  if (o.use_tensor_cores && rows >= DD_EXPERIMENT_TC_MIN_ROWS && c.head_dim == 128 && c.kv_dtype != DD_DTYPE_F32 &&
+  if (tc && rows >= DD_EXPERIMENT_TC_MIN_ROWS) return kItemTc;
 #else
-  if (o.use_tensor_cores && rows >= 128 && c.head_dim == 128 && c.kv_dtype != DD_DTYPE_F32 &&
+  if (tc && rows >= 128) return kItemTc;
 #endif
-      dd_tc_available())
-    return kItemTc;
   return kItemMma;
 }
 
-static int row_tile_for(int kind) { return kind == kItemTc ? 256 : kind == kItemMma ? 16 : 64; }
+static int row_tile_for(int kind) {
+  return kind == kItemTc2 ? 512 : kind == kItemTc ? 256 : kind == kItemMma ? 16 : 64;
+}
 
 // SMs of the target GPU (B200); only a load-balancing heuristic, so the
 // planner needs no device.
@@ -267,7 +269,7 @@ static void build_items(dd_plan* p) {
     const int kind = kind_for(c, p->opts, rows);
     const int rt = row_tile_for(kind);
     p->kv_tokens_by_kind[kind] += n.num_tokens;
-    if (kind == kItemTc) p->tc_row_tokens += rows * n.num_tokens * Hkv;  // all KV heads
+    if (kind == kItemTc || kind == kItemTc2) p->tc_row_tokens += rows * n.num_tokens * Hkv;  // all KV heads
     const int64_t row_tiles = (rows + rt - 1) / rt;
     // Split-K chunking. Each extra chunk costs one more partial state per
     // (query, head) written and read back by the merge; allow at most 1/8 of
@@ -278,12 +280,13 @@ static void build_items(dd_plan* p) {
     int64_t chunk_pages = p->opts.max_chunk_pages > 0 ? p->opts.max_chunk_pages
                           : (row_tiles == 1 ? 16 : (int64_t)1 << 30);
     int64_t k = std::min<int64_t>(kmax, (n.page_count + chunk_pages - 1) / chunk_pages);
-    if (kind == kItemTc && p->opts.max_chunk_pages <= 0) {
+    if ((kind == kItemTc || kind == kItemTc2) && p->opts.max_chunk_pages <= 0) {
       // Wide nodes are compute-bound: split their pages so the tensor-core
       // grid covers the SMs (at least 32 pages per chunk), even though each
-      // chunk adds a partial state per row.
+      // chunk adds a partial state per row. A CTA-pair item takes two SMs.
       const int64_t per = row_tiles * Hkv;
-      const int64_t target = std::max<int64_t>(1, (kPlanSms + per / 2) / per);
+      const int64_t units = kind == kItemTc2 ? kPlanSms / 2 : kPlanSms;
+      const int64_t target = std::max<int64_t>(1, (units + per / 2) / per);
       k = std::max<int64_t>(k, std::min<int64_t>({target, (int64_t)4, std::max<int64_t>(1, n.page_count / 32)}));
     }
     k = std::max<int64_t>(1, std::min<int64_t>(k, n.page_count));
@@ -412,7 +415,7 @@ int dd_plan_get_info(const dd_plan* p, dd_plan_info* info) {
   info->max_depth = p->max_depth;
   info->kv_tokens = p->kv_tokens;
   info->kv_tokens_flat = p->kv_tokens_flat;
-  for (int k = 0; k < 3; ++k) info->kv_tokens_by_kernel[k] = p->kv_tokens_by_kind[k];
+  for (int k = 0; k < kNumItemKinds; ++k) info->kv_tokens_by_kernel[k] = p->kv_tokens_by_kind[k];
   info->tc_row_tokens = p->tc_row_tokens;
   info->workspace_bytes = plan_workspace_bytes(p);
   info->device_bytes = p->image.size();

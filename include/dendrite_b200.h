@@ -121,7 +121,8 @@ typedef struct dd_plan_options {
   int32_t share_prefixes;  /* 1: cascade over shared prefixes; 0: flat per-query plan */
   int32_t max_chunk_pages; /* 0 = automatic split-K chunking */
   int32_t use_tensor_cores;/* 1 (default): tcgen05 path for nodes with many rows */
-  int32_t reserved;
+  int32_t cta_pairs;        /* 1: nodes of > 256 rows run on CTA pairs (cta_group::2
+                             * tcgen05 kernel, bf16 only); 0 (default): one-SM kernel */
 } dd_plan_options;
 
 typedef struct dd_plan_info {
@@ -134,8 +135,9 @@ typedef struct dd_plan_info {
   size_t workspace_bytes;  /* required size of `workspace` */
   size_t device_bytes;     /* required size of the buffer given to dd_plan_upload */
   /* Unique KV tokens read by each attention kernel: [0] CUDA-core kernel,
-   * [1] streaming tensor-core (mma) kernel, [2] tcgen05 kernel (wide nodes). */
-  int64_t kv_tokens_by_kernel[3];
+   * [1] streaming tensor-core (mma) kernel, [2] tcgen05 kernel (wide nodes),
+   * [3] tcgen05 kernel on CTA pairs (the widest nodes). */
+  int64_t kv_tokens_by_kernel[4];
   /* Sum over tcgen05 nodes and KV heads of (query rows x tokens): the
    * kernel's 4 * head_dim FLOPs per unit (Q.K^T and P.V). */
   int64_t tc_row_tokens;

@@ -61,7 +61,7 @@ def test_single_token_returns_dequantised_v(cuda, fmt, tc):
     torch.cuda.synchronize()
     prof = _lib.profile_read()
     _lib.profile_enable(False)
-    assert (prof["attn_tc"][1] == 1) == tc, prof
+    assert (prof["attn_tc"][1] >= 1) == tc, prof
     got = out.view(torch.int16).cpu().numpy().view(np.uint16)
     deq = oracle.dequantize(codes, scales, fmt, out="f32")
     ref, _ = oracle.decode_batch(bits_to_f32(q), deq, indptr, ids, ntok, HKV)

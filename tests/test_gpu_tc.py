@@ -16,9 +16,10 @@ def _dev_bf16(bits, dev):
     return torch.from_numpy(bits.view(np.int16).copy()).view(torch.bfloat16).to(dev)
 
 
-def _run(tb, pool_bits, q_bits, dev, tc=True, gqa=0):
+def _run(tb, pool_bits, q_bits, dev, tc=True, gqa=0, pairs=False):
     cfg = dd.make_config(tb.num_qo_heads, tb.num_kv_heads, tb.head_dim, tb.num_pages, gqa_map=gqa)
-    plan = dd.CascadePlan(cfg, tb.indptr, tb.block_ids, tb.num_tokens, use_tensor_cores=tc)
+    plan = dd.CascadePlan(cfg, tb.indptr, tb.block_ids, tb.num_tokens, use_tensor_cores=tc,
+                          cta_pairs=pairs)
     plan.upload(dev)
     launches = _lib.launch_count()
     _lib.profile_enable(True)
@@ -61,15 +62,17 @@ CASES = [
 ]
 
 
+@pytest.mark.parametrize("pairs", [False, True])
 @pytest.mark.parametrize("Hq,Hkv,prefix,leaves,suffix,gqa", CASES)
-def test_wide_root_vs_oracle(cuda, Hq, Hkv, prefix, leaves, suffix, gqa):
+def test_wide_root_vs_oracle(cuda, Hq, Hkv, prefix, leaves, suffix, gqa, pairs):
+    """pairs: nodes of > 256 rows on the CTA-pair (cta_group::2) kernel."""
     seed = Hq + prefix + leaves
     tb = wl.build_tree("wide", Hq, Hkv, 128, prefix, [], leaves, suffix, seed)
     rng = np.random.default_rng(seed)
     pool = bf16_bits(random_pool(rng, tb.num_pages, Hkv, 128))
     q = bf16_bits(rng.standard_normal((tb.batch_size, Hq, 128)).astype(np.float32))
-    got, lse, prof, _ = _run(tb, pool, q, cuda, gqa=gqa)
-    assert prof["attn_tc"][1] == 1, prof  # the wide root went through tcgen05
+    got, lse, prof, _ = _run(tb, pool, q, cuda, gqa=gqa, pairs=pairs)
+    assert prof["attn_tc"][1] >= 1, prof  # the wide root went through tcgen05
     ref, ref_lse = oracle.decode_batch(bits_to_f32(q), pool, tb.indptr, tb.block_ids,
                                        tb.num_tokens, Hkv, gqa_grouped=bool(gqa))
     assert_close(got, bits_to_f32(bf16_bits(ref)), what="tc root")
@@ -83,7 +86,7 @@ def test_shared_partial_last_page_through_tc(cuda):
     pool = bf16_bits(random_pool(rng, P, 8, 128))
     q = bf16_bits(rng.standard_normal((len(ntok), 32, 128)).astype(np.float32))
     got, lse, prof, _ = _run(tb, pool, q, cuda)
-    assert prof["attn_tc"][1] == 1
+    assert prof["attn_tc"][1] >= 1
     ref, ref_lse = oracle.decode_batch(bits_to_f32(q), pool, indptr, ids, ntok, 8)
     assert_close(got, bits_to_f32(bf16_bits(ref)), what="partial pages")
     np.testing.assert_allclose(lse, ref_lse, atol=2e-3)
@@ -96,7 +99,7 @@ def test_tc_matches_mma_path(cuda):
     q = bf16_bits(rng.standard_normal((tb.batch_size, 32, 128)).astype(np.float32))
     a, la, pa, _ = _run(tb, pool, q, cuda, tc=True)
     b, lb, pb, _ = _run(tb, pool, q, cuda, tc=False)
-    assert pa["attn_tc"][1] == 1 and pb["attn_tc"][1] == 0
+    assert pa["attn_tc"][1] >= 1 and pb["attn_tc"][1] == 0
     assert_close(a, b, what="tc vs mma")
     np.testing.assert_allclose(la, lb, atol=1e-3)
 
@@ -115,21 +118,22 @@ def test_large_score_range_rescales(cuda):
     pool = bf16_bits(x)
     q = bf16_bits(rng.standard_normal((len(ntok), 32, 128)).astype(np.float32))
     got, lse, prof, _ = _run(tb, pool, q, cuda)
-    assert prof["attn_tc"][1] == 1
+    assert prof["attn_tc"][1] >= 1
     ref, ref_lse = oracle.decode_batch(bits_to_f32(q), pool, indptr, ids, ntok, 8)
     assert_close(got, bits_to_f32(bf16_bits(ref)), what="rescale")
     np.testing.assert_allclose(lse, ref_lse, rtol=1e-4, atol=1e-2)
 
 
-def test_mcts_subset_vs_oracle(cuda):
+@pytest.mark.parametrize("pairs", [False, True])
+def test_mcts_subset_vs_oracle(cuda, pairs):
     """A 128-leaf version of the MCTS tree (root through tcgen05), all queries."""
     tb = wl.build_tree("mcts128", 32, 8, 128, 8192, [(4, 128, 1024), (4, 128, 1024), (2, 128, 1024)],
                        4, (16, 256), 0xD3D1)
     rng = np.random.default_rng(1)
     pool = bf16_bits(random_pool(rng, tb.num_pages, 8, 128))
     q = bf16_bits(rng.standard_normal((tb.batch_size, 32, 128)).astype(np.float32))
-    got, lse, prof, n = _run(tb, pool, q, cuda)
-    assert prof["attn_tc"][1] == 1 and n >= 3
+    got, lse, prof, n = _run(tb, pool, q, cuda, pairs=pairs)
+    assert prof["attn_tc"][1] >= 1 and n >= 3
     ref, ref_lse = oracle.decode_batch(bits_to_f32(q), pool, tb.indptr, tb.block_ids, tb.num_tokens, 8)
     assert_close(got, bits_to_f32(bf16_bits(ref)), what="mcts128")
     np.testing.assert_allclose(lse, ref_lse, atol=2e-3)
@@ -161,7 +165,7 @@ def test_fp8_wide_root_vs_oracle(cuda, fmt, prefix, gqa):
         torch.cuda.synchronize()
         prof = _lib.profile_read()
         _lib.profile_enable(False)
-        assert (prof["attn_tc"][1] == 1) == tc, prof
+        assert (prof["attn_tc"][1] >= 1) == tc, prof
         outs[tc] = (out.float().cpu().numpy(), lse.cpu().numpy())
     deq = oracle.dequantize(codes.cpu().numpy(), scales.cpu().numpy(), fmt)
     ref, ref_lse = oracle.decode_batch(bits_to_f32(q), deq, tb.indptr, tb.block_ids, tb.num_tokens, 8,
