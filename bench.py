@@ -452,18 +452,20 @@ def run_tree(args, world, rank, local, dev):
         traffic = json.loads(tf.read_text()).get(f"{args.workload}:{attn_kind}")
 
     # End-to-end through the public API with host buffers: plan from the host
-    # block tables, H2D of the plan and the queries, decode (and, for the head
-    # split, the all-gather), D2H of the output.
+    # block tables (dd_plan_rebuild), H2D of the plan and the queries, decode
+    # (and, for the head split, the all-gather), D2H of the output.
     q_host = q_local.cpu().pin_memory()
     res = out if heads else out_local
     out_host = torch.empty(res.shape, dtype=res.dtype).pin_memory()
     q_dev2 = torch.empty_like(q_local)
+    # The engine keeps one plan object and re-plans it every decode step.
+    p2 = dd.CascadePlan(lcfg, tb.indptr, tb.block_ids, tb.num_tokens)
+    p2.device_buffer = plan.device_buffer
 
     def e2e_step():
-        p2 = dd.CascadePlan(lcfg, tb.indptr, tb.block_ids, tb.num_tokens)
-        p2.device_buffer = plan.device_buffer
+        q_dev2.copy_(q_host, non_blocking=True)  # in flight while the host plans
+        p2.rebuild(tb.indptr, tb.block_ids, tb.num_tokens)
         p2.upload(dev)
-        q_dev2.copy_(q_host, non_blocking=True)
         r = decode(p2, q_dev2)
         out_host.copy_(r, non_blocking=True)
         torch.cuda.synchronize()

@@ -146,6 +146,19 @@ class CascadePlan:
         ntok = np.array([t.num_tokens() for t in tables], dtype=np.int32)
         return cls(cfg, indptr, ids, ntok, **kw)
 
+    def rebuild(self, indptr, block_ids, num_tokens) -> "CascadePlan":
+        """Re-plan for a new batch in place (dd_plan_rebuild); the device
+        buffer is kept and must be uploaded again."""
+        self._indptr = np.ascontiguousarray(indptr, dtype=np.int32)
+        self._ids = np.ascontiguousarray(block_ids, dtype=np.uint32)
+        self._ntok = np.ascontiguousarray(num_tokens, dtype=np.int32)
+        self.batch_size = len(self._ntok)
+        rc = lib.dd_plan_rebuild(self._h, self.batch_size, self._indptr.ctypes.data_as(_lib._I32P),
+                                 self._ids.ctypes.data_as(_lib._U32P) if len(self._ids) else None,
+                                 self._ntok.ctypes.data_as(_lib._I32P))
+        check(rc, "dd_plan_rebuild")
+        return self
+
     def __del__(self):
         h = getattr(self, "_h", None)
         if h:

@@ -65,6 +65,10 @@ struct Node {
 
 }  // namespace dd
 
+namespace dd {
+struct PlanScratch;  // planner.cpp: working buffers kept across dd_plan_rebuild
+}
+
 // The opaque plan handed across the C ABI.
 struct dd_plan {
   dd_attn_config cfg;
@@ -89,6 +93,8 @@ struct dd_plan {
   // Set by dd_plan_upload.
   const void* device_base = nullptr;
   int device_id = -1;
+  dd::PlanScratch* scratch = nullptr;
+  ~dd_plan();
 };
 
 namespace dd {

@@ -95,11 +95,49 @@ static int row_tile_for(int kind) {
 // planner needs no device.
 constexpr int kPlanSms = 148;
 
+// A radix-tree node: a run [off, off + len) of one source table.
+struct Run {
+  int32_t q, off, len;          // source table and run within it
+  int32_t first_child = -1, last_child = -1, next_sibling = -1;
+  int32_t ends_head = -1, ends_tail = -1;  // queries whose table ends here
+};
+
+// Working buffers of one planning pass. A plan keeps them (and all its
+// arrays) across dd_plan_rebuild, so re-planning every decode step reuses
+// memory instead of allocating and faulting in fresh pages.
+struct PlanScratch {
+  std::vector<int32_t> used, end_next, node_k, node_slot0, node_kind, qcount, qcursor;
+  std::vector<Run> runs;
+  struct Frame {
+    int32_t node;   // plan node index (-1 for the root)
+    int32_t child;  // next child run to descend into
+  };
+  std::vector<Frame> stack;
+  std::vector<std::pair<int64_t, int32_t>> keys;
+};
+
+static void reset_plan(dd_plan* p) {
+  p->nodes.clear();
+  p->pages.clear();
+  p->query_order.clear();
+  p->path_indptr.clear();
+  p->path_slots.clear();
+  for (auto& v : p->items) v.clear();
+  p->num_slots = p->kv_tokens = p->kv_tokens_flat = p->tc_row_tokens = 0;
+  for (auto& k : p->kv_tokens_by_kind) k = 0;
+  p->max_depth = 0;
+  p->device_base = nullptr;
+  p->device_id = -1;
+  if (!p->scratch) p->scratch = new PlanScratch();
+}
+
 // Builds nodes / pages / query_order from the tables.
 static int build_nodes(dd_plan* p, const int32_t* indptr, const uint32_t* ids,
                        const int32_t* ntok) {
   const int B = p->batch_size;
-  std::vector<int32_t> used(B);
+  PlanScratch& sc = *p->scratch;
+  std::vector<int32_t>& used = sc.used;
+  used.assign(B, 0);
   for (int b = 0; b < B; ++b) {
     const int nb = indptr[b + 1] - indptr[b];
     if (nb < 0) return fail(DD_ERR_INVALID_ARGUMENT, "block_indptr must be non-decreasing");
@@ -107,14 +145,22 @@ static int build_nodes(dd_plan* p, const int32_t* indptr, const uint32_t* ids,
       return fail(DD_ERR_INVALID_ARGUMENT,
                   "num_tokens[" + std::to_string(b) + "] exceeds its block table");
     used[b] = (ntok[b] + kPageSize - 1) / kPageSize;
-    for (int i = 0; i < used[b]; ++i) {
-      const uint32_t id = ids[indptr[b] + i];
-      if ((int64_t)id >= (int64_t)p->cfg.num_pages)
-        // DendriteError::InvalidBlock (crates/dendrite-core/src/error.rs:15-17)
-        return fail(DD_ERR_INVALID_ARGUMENT, "invalid block id: " + std::to_string(id));
-    }
     p->kv_tokens_flat += ntok[b];
   }
+  // Block ids must be < num_pages (DendriteError::InvalidBlock,
+  // crates/dendrite-core/src/error.rs:15-17). Every position of a table is
+  // either the first occurrence of a run (checked when the run is created) or
+  // equal to such a position, so checking new runs covers all ids.
+  const uint32_t num_pages = (uint32_t)p->cfg.num_pages;
+  auto check_ids = [&](const uint32_t* x, int n) -> int {
+    uint32_t mx = 0;
+    for (int i = 0; i < n; ++i) mx = std::max(mx, x[i]);
+    if (n > 0 && mx >= num_pages) {
+      for (int i = 0; i < n; ++i)
+        if (x[i] >= num_pages) return fail(DD_ERR_INVALID_ARGUMENT, "invalid block id: " + std::to_string(x[i]));
+    }
+    return DD_OK;
+  };
   auto valid_of = [&](int b, int i) {
     return (i == used[b] - 1 && ntok[b] % kPageSize) ? ntok[b] % kPageSize : kPageSize;
   };
@@ -125,6 +171,7 @@ static int build_nodes(dd_plan* p, const int32_t* indptr, const uint32_t* ids,
     for (int b = 0; b < B; ++b) {
       p->query_order[b] = b;
       if (used[b] == 0) continue;
+      if (int st = check_ids(ids + indptr[b], used[b])) return st;
       Node n;
       n.q_begin = b;
       n.num_q = 1;
@@ -142,15 +189,12 @@ static int build_nodes(dd_plan* p, const int32_t* indptr, const uint32_t* ids,
   // Radix tree over (page id, valid tokens) sequences. A node is a run of
   // positions [off, off + len) of one source table; inserting a table walks
   // runs with plain element compares and splits a run where the tables part.
-  struct Run {
-    int32_t q, off, len;          // source table and run within it
-    int32_t first_child = -1, last_child = -1, next_sibling = -1;
-    int32_t ends_head = -1, ends_tail = -1;  // queries whose table ends here
-  };
-  std::vector<Run> runs;
+  std::vector<Run>& runs = sc.runs;
+  runs.clear();
   runs.reserve(2 * (size_t)B + 1);
   runs.push_back(Run{-1, 0, 0});
-  std::vector<int32_t> end_next(B, -1);
+  std::vector<int32_t>& end_next = sc.end_next;
+  end_next.assign(B, -1);
   auto key_eq = [&](int qa, int ia, int qb, int ib) {
     return ids[indptr[qa] + ia] == ids[indptr[qb] + ib] && valid_of(qa, ia) == valid_of(qb, ib);
   };
@@ -175,6 +219,7 @@ static int build_nodes(dd_plan* p, const int32_t* indptr, const uint32_t* ids,
       int32_t c = runs[cur].first_child;
       while (c >= 0 && !key_eq(runs[c].q, runs[c].off, b, pos)) c = runs[c].next_sibling;
       if (c < 0) {
+        if (int st = check_ids(ids + indptr[b] + pos, used[b] - pos)) return st;
         const int32_t nid = (int32_t)runs.size();
         runs.push_back(Run{b, pos, used[b] - pos});
         add_child(cur, nid);
@@ -189,13 +234,16 @@ static int build_nodes(dd_plan* p, const int32_t* indptr, const uint32_t* ids,
         // differ only at either table's last page.
         const uint32_t* x = ids + indptr[rc.q] + rc.off;
         const uint32_t* y = ids + indptr[b] + pos;
-        while (k < lim && x[k] == y[k]) ++k;
-        for (int t = 1; t < k; ++t)
-          if (rc.off + t == used[rc.q] - 1 || pos + t == used[b] - 1)
-            if (valid_of(rc.q, rc.off + t) != valid_of(b, pos + t)) {
-              k = t;
-              break;
-            }
+        // Usually the whole run matches (a shared prefix): one compare.
+        if (lim > 1 && std::memcmp(x + 1, y + 1, (size_t)(lim - 1) * sizeof(uint32_t)) == 0) {
+          k = lim;
+        } else {
+          while (k + 8 <= lim && std::memcmp(x + k, y + k, 8 * sizeof(uint32_t)) == 0) k += 8;
+          while (k < lim && x[k] == y[k]) ++k;
+        }
+        // Valid counts can differ only at either table's last page.
+        for (const int t : {used[rc.q] - 1 - rc.off, used[b] - 1 - pos})
+          if (t >= 1 && t < k && valid_of(rc.q, rc.off + t) != valid_of(b, pos + t)) k = t;
       }
       if (k < rc.len) {
         // Split c after k positions: the tail keeps c's children and ends.
@@ -220,14 +268,11 @@ static int build_nodes(dd_plan* p, const int32_t* indptr, const uint32_t* ids,
   // before its children's, so each node's queries are a contiguous range.
   p->query_order.reserve(B);
   for (int32_t b = runs[0].ends_head; b >= 0; b = end_next[b]) p->query_order.push_back(b);
-  struct Frame {
-    int32_t node;   // plan node index (-1 for the root)
-    int32_t child;  // next child run to descend into
-  };
-  std::vector<Frame> stack;
+  std::vector<PlanScratch::Frame>& stack = sc.stack;
+  stack.clear();
   stack.push_back({-1, runs[0].first_child});
   while (!stack.empty()) {
-    Frame& f = stack.back();
+    PlanScratch::Frame& f = stack.back();
     if (f.child >= 0) {
       const int32_t r = f.child;
       f.child = runs[r].next_sibling;
@@ -261,9 +306,19 @@ static void build_items(dd_plan* p) {
   const dd_attn_config& c = p->cfg;
   const int Hq = c.num_qo_heads, Hkv = c.num_kv_heads, g = Hq / Hkv, D = c.head_dim;
   const double elem = c.kv_dtype == DD_DTYPE_F32 ? 4.0 : c.kv_dtype == DD_DTYPE_BF16 ? 2.0 : 1.0;
-  std::vector<std::vector<int32_t>> qslots(p->batch_size);
+  PlanScratch& sc = *p->scratch;
+  const size_t N = p->nodes.size();
+  const int B = p->batch_size;
+  sc.node_k.assign(N, 1);
+  sc.node_slot0.assign(N, 0);
+  sc.node_kind.assign(N, 0);
+  sc.keys.resize(N);
+  sc.qcount.assign((size_t)B + 1, 0);  // difference array, then path lengths
+  int64_t n_items[kNumItemKinds] = {0, 0, 0, 0};
+  // Pass 1: kernel kind, split-K chunk count and slots of every node.
   p->num_slots = 0;
-  for (const Node& n : p->nodes) {
+  for (size_t ni = 0; ni < N; ++ni) {
+    const Node& n = p->nodes[ni];
     p->kv_tokens += n.num_tokens;
     const int64_t rows = (int64_t)n.num_q * g;
     const int kind = kind_for(c, p->opts, rows);
@@ -290,13 +345,53 @@ static void build_items(dd_plan* p) {
       k = std::max<int64_t>(k, std::min<int64_t>({target, (int64_t)4, std::max<int64_t>(1, n.page_count / 32)}));
     }
     k = std::max<int64_t>(1, std::min<int64_t>(k, n.page_count));
-    for (int64_t ci = 0; ci < k; ++ci) {
-      const int32_t pb = (int32_t)(ci * n.page_count / k);
-      const int32_t pe = (int32_t)((ci + 1) * n.page_count / k);
-      const int32_t slot_base = (int32_t)p->num_slots;
-      p->num_slots += (int64_t)n.num_q * Hq;
+    sc.node_k[ni] = (int32_t)k;
+    sc.node_kind[ni] = kind;
+    // Item size of this node for the longest-first order: pages per chunk x
+    // rows per tile.
+    sc.keys[ni] = {-((n.page_count + k - 1) / k) * std::min<int64_t>(rows, rt), (int32_t)ni};
+    sc.node_slot0[ni] = (int32_t)p->num_slots;
+    p->num_slots += k * n.num_q * Hq;
+    n_items[kind] += k * Hkv * row_tiles;
+    sc.qcount[n.q_begin] += (int32_t)k;
+    sc.qcount[n.q_begin + n.num_q] -= (int32_t)k;
+  }
+  // Each query's path entries in root-to-leaf order (nodes are in DFS
+  // pre-order), as CSR: lengths from the difference array, then fill.
+  p->path_indptr.assign((size_t)B + 1, 0);
+  int32_t run = 0;
+  for (int q = 0; q < B; ++q) {
+    run += sc.qcount[q];
+    p->path_indptr[q + 1] = p->path_indptr[q] + run;
+  }
+  p->path_slots.resize(p->path_indptr[B]);
+  sc.qcursor.assign(p->path_indptr.begin(), p->path_indptr.end() - 1);
+  for (int k = 0; k < kNumItemKinds; ++k) p->items[k].reserve(n_items[k]);
+  // Pass 2: path slots, in DFS order.
+  for (size_t ni = 0; ni < N; ++ni) {
+    const Node& n = p->nodes[ni];
+    for (int32_t ci = 0; ci < sc.node_k[ni]; ++ci) {
+      const int32_t slot_base = sc.node_slot0[ni] + ci * n.num_q * Hq;
       for (int32_t qi = 0; qi < n.num_q; ++qi)
-        qslots[n.q_begin + qi].push_back(slot_base + qi * Hq);
+        p->path_slots[sc.qcursor[n.q_begin + qi]++] = slot_base + qi * Hq;
+    }
+  }
+  // Pass 3: items, longest first (LPT) so the big shared nodes start early:
+  // nodes in decreasing item size (ties in DFS order), each node's items
+  // together.
+  std::sort(sc.keys.begin(), sc.keys.end());
+  for (const auto& key : sc.keys) {
+    const size_t ni = (size_t)key.second;
+    const Node& n = p->nodes[ni];
+    const int64_t rows = (int64_t)n.num_q * g;
+    const int kind = sc.node_kind[ni];
+    const int rt = row_tile_for(kind);
+    const int64_t row_tiles = (rows + rt - 1) / rt;
+    const int32_t k = sc.node_k[ni];
+    for (int32_t ci = 0; ci < k; ++ci) {
+      const int32_t pb = (int32_t)((int64_t)ci * n.page_count / k);
+      const int32_t pe = (int32_t)((int64_t)(ci + 1) * n.page_count / k);
+      const int32_t slot_base = sc.node_slot0[ni] + ci * n.num_q * Hq;
       for (int h = 0; h < Hkv; ++h)
         for (int64_t t = 0; t < row_tiles; ++t) {
           WorkItem it;
@@ -312,16 +407,6 @@ static void build_items(dd_plan* p) {
         }
     }
   }
-  // Longest items first so the big shared nodes start early (LPT order).
-  for (auto& v : p->items)
-    std::stable_sort(v.begin(), v.end(), [](const WorkItem& a, const WorkItem& b) {
-      return (int64_t)a.npages * a.nrows > (int64_t)b.npages * b.nrows;
-    });
-  p->path_indptr.assign(p->batch_size + 1, 0);
-  for (int i = 0; i < p->batch_size; ++i)
-    p->path_indptr[i + 1] = p->path_indptr[i] + (int32_t)qslots[i].size();
-  p->path_slots.reserve(p->path_indptr[p->batch_size]);
-  for (auto& v : qslots) p->path_slots.insert(p->path_slots.end(), v.begin(), v.end());
 }
 
 static void pack_image(dd_plan* p) {
@@ -337,7 +422,8 @@ static void pack_image(dd_plan* p) {
   p->off_qorder = take(p->query_order.size() * sizeof(int32_t));
   p->off_pindptr = take(p->path_indptr.size() * sizeof(int32_t));
   p->off_pslots = take(p->path_slots.size() * sizeof(int32_t));
-  p->image.assign(std::max<size_t>(off, kAlign), 0);
+  // Reused across rebuilds; alignment gaps are never read.
+  p->image.resize(std::max<size_t>(off, kAlign));
   auto put = [&](size_t o, const void* src, size_t n) {
     if (n) std::memcpy(p->image.data() + o, src, n);
   };
@@ -350,6 +436,8 @@ static void pack_image(dd_plan* p) {
 }
 
 }  // namespace dd
+
+dd_plan::~dd_plan() { delete scratch; }
 
 using namespace dd;
 
@@ -384,6 +472,7 @@ int dd_plan_create(const dd_attn_config* cfg, int32_t batch_size, const int32_t*
   }
   p->batch_size = batch_size;
   try {
+    reset_plan(p);
     st = build_nodes(p, block_indptr, block_ids, num_tokens);
     if (st) {
       delete p;
@@ -401,6 +490,36 @@ int dd_plan_create(const dd_attn_config* cfg, int32_t batch_size, const int32_t*
   }
   *out_plan = p;
   return DD_OK;
+}
+
+int dd_plan_rebuild(dd_plan* p, int32_t batch_size, const int32_t* block_indptr,
+                    const uint32_t* block_ids, const int32_t* num_tokens) {
+  if (!p) return fail(DD_ERR_INVALID_ARGUMENT, "plan is NULL");
+  if (batch_size < 0) return fail(DD_ERR_INVALID_ARGUMENT, "batch_size must be >= 0");
+  if (batch_size > 0 && (!block_indptr || !num_tokens))
+    return fail(DD_ERR_INVALID_ARGUMENT, "block_indptr / num_tokens is NULL");
+  if (batch_size > 0 && block_indptr[batch_size] > 0 && !block_ids)
+    return fail(DD_ERR_INVALID_ARGUMENT, "block_ids is NULL");
+  p->batch_size = batch_size;
+  try {
+    reset_plan(p);
+    int st = build_nodes(p, block_indptr, block_ids, num_tokens);
+    if (!st) {
+      build_items(p);
+      if (p->num_slots > INT32_MAX) st = fail(DD_ERR_INVALID_ARGUMENT, "plan too large (partial slots exceed 2^31)");
+    }
+    if (!st) pack_image(p);
+    if (st) {
+      reset_plan(p);  // leave an empty, valid plan behind
+      p->batch_size = 0;
+      pack_image(p);
+    }
+    return st;
+  } catch (const std::bad_alloc&) {
+    reset_plan(p);
+    p->batch_size = 0;
+    return fail(DD_ERR_ALLOCATION, "host allocation failed while planning");
+  }
 }
 
 void dd_plan_destroy(dd_plan* plan) { delete plan; }

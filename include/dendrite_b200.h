@@ -148,6 +148,13 @@ int dd_plan_create(const dd_attn_config* cfg, int32_t batch_size,
                    const int32_t* num_tokens, const dd_plan_options* opts,
                    dd_plan** out_plan);
 void dd_plan_destroy(dd_plan* plan);
+/* Re-plans an existing plan for a new decode batch (same config and
+ * options), reusing its host memory: the per-step call of an engine whose
+ * tree grows by one token per leaf per step. The device image must be
+ * uploaded again (dd_plan_upload) before the next dd_cascade_decode. On
+ * error the plan is left empty (batch 0). No reference counterpart. */
+int dd_plan_rebuild(dd_plan* plan, int32_t batch_size, const int32_t* block_indptr,
+                    const uint32_t* block_ids, const int32_t* num_tokens);
 int dd_plan_get_info(const dd_plan* plan, dd_plan_info* info);
 /* Copies the plan's arrays into caller-owned device memory (>= device_bytes,
  * 256-byte aligned). Must be called before dd_cascade_decode. */

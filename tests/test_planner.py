@@ -163,3 +163,33 @@ def test_cascade_decomposition_equals_flat_reference(seed):
                     acc_o[qq, h], acc_l[qq, h] = mo[0], ml[0]
     np.testing.assert_allclose(acc_o, ref, atol=2e-5)
     np.testing.assert_allclose(acc_l, ref_lse, atol=2e-5)
+
+
+def test_rebuild_matches_fresh_plan():
+    """dd_plan_rebuild (re-planning into a live plan) gives the same plan as
+    dd_plan_create, across batches of different shapes, and an invalid batch
+    leaves an empty plan."""
+    import dendrite_b200 as dd
+    from dendrite_b200 import workloads as wl
+
+    trees = [wl.small_tree(s, Hq=8, Hkv=2, D=64, prefix=200 + 16 * s, leaves_per_node=2 + s % 3)
+             for s in range(4)]
+    P = max(t.num_pages for t in trees)
+    cfg = dd.make_config(8, 2, 64, P)
+    live = dd.CascadePlan(cfg, trees[0].indptr, trees[0].block_ids, trees[0].num_tokens)
+    for t in trees + trees[::-1]:
+        live.rebuild(t.indptr, t.block_ids, t.num_tokens)
+        fresh = dd.CascadePlan(cfg, t.indptr, t.block_ids, t.num_tokens)
+        a, b = live.info(), fresh.info()
+        for f in ("batch_size", "num_nodes", "num_items", "max_depth", "kv_tokens", "workspace_bytes",
+                  "device_bytes", "tc_row_tokens"):
+            assert getattr(a, f) == getattr(b, f), f
+        assert list(a.kv_tokens_by_kernel) == list(b.kv_tokens_by_kernel)
+        na, nb = live.nodes(), fresh.nodes()
+        for k in nb:
+            assert np.array_equal(na[k], nb[k]), k
+    bad = trees[0].block_ids.copy()
+    bad[0] = P + 5
+    with pytest.raises(dd.InvalidArgument):
+        live.rebuild(trees[0].indptr, bad, trees[0].num_tokens)
+    assert live.info().batch_size == 0 and live.info().num_items == 0
