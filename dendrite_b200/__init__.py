@@ -9,7 +9,8 @@ if it is missing: there is no CPU fallback.
 from ._lib import (AllocationFailed, CudaError, FfiError, InvalidArgument, NotAvailable,  # noqa: F401
                    WorkspaceTooSmall, version)
 from .backend import (PAGE_SIZE, SUPPORTED_HEAD_DIMS, AttentionConfig, B200Backend,  # noqa: F401
-                      BlockTable, CascadePlan, cascade_decode, decode_paged, dequantize_kv_pages,
+                      BlockTable, CascadePlan, append_kv_batch, cascade_decode, copy_pages,
+                      decode_paged, dequantize_kv_pages,
                       make_config, merge_states, quantize_kv_pages, scatter_head_shards,
                       workspace_status)
 

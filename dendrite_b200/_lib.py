@@ -113,6 +113,8 @@ SIGNATURES = {
     "dd_quantize_workspace_size": (C.c_size_t, [_QCP]),
     "dd_quantize_kv_pages": (C.c_int, [_QCP, _VP, C.c_int64, _VP, _VP, _VP, C.c_size_t, _VP]),
     "dd_dequantize_kv_pages": (C.c_int, [_QCP, _VP, _VP, C.c_int64, _VP, C.c_int32, _VP]),
+    "dd_append_kv_batch": (C.c_int, [_CFGP, _VP, _VP, C.c_int32, _VP, _VP, _VP, _VP, C.c_int32, _VP, _VP]),
+    "dd_copy_pages": (C.c_int, [_CFGP, _VP, _VP, C.c_int32, _VP, _VP, _VP, _VP]),
     "dd_scatter_head_shards": (C.c_int, [_CFGP, C.c_int32, C.c_int32, _VP, _VP, _VP]),
     "dd_allgather_heads": (C.c_int, [_VP, _CFGP, C.c_int32, C.c_int32, _VP, _VP, _VP, _VP]),
     "dd_tc_available": (C.c_int, []),

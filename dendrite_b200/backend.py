@@ -307,6 +307,25 @@ def dequantize_kv_pages(codes: torch.Tensor, scales: torch.Tensor, fmt: str,
     return out
 
 
+def append_kv_batch(cfg: AttnConfig, kv_pages: torch.Tensor, kv_scales: torch.Tensor | None,
+                    page_ids: torch.Tensor, slots: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                    status: torch.Tensor | None = None, stream=None) -> None:
+    """Append token i of k, v [n, Hkv, D] (bf16 or f32) to slot slots[i] of
+    page page_ids[i] (device int tensors), quantizing for FP8 pools."""
+    src = DTYPE_F32 if k.dtype == torch.float32 else DTYPE_BF16
+    check(lib.dd_append_kv_batch(C.byref(cfg), _ptr(kv_pages), _ptr(kv_scales), k.shape[0],
+                                 _ptr(page_ids), _ptr(slots), _ptr(k), _ptr(v), src, _ptr(status),
+                                 _stream(stream)), "dd_append_kv_batch")
+
+
+def copy_pages(cfg: AttnConfig, kv_pages: torch.Tensor, kv_scales: torch.Tensor | None,
+               src: torch.Tensor, dst: torch.Tensor, status: torch.Tensor | None = None,
+               stream=None) -> None:
+    """Copy-on-write data copy: page dst[i] <- page src[i]."""
+    check(lib.dd_copy_pages(C.byref(cfg), _ptr(kv_pages), _ptr(kv_scales), src.numel(), _ptr(src),
+                            _ptr(dst), _ptr(status), _stream(stream)), "dd_copy_pages")
+
+
 def scatter_head_shards(cfg: AttnConfig, world: int, gathered: torch.Tensor, out: torch.Tensor,
                         stream=None) -> torch.Tensor:
     check(lib.dd_scatter_head_shards(C.byref(cfg), world, out.shape[0], _ptr(gathered), _ptr(out),

@@ -251,6 +251,27 @@ int dd_append_kv(const dd_attn_config* cfg, void* kv_pages, uint32_t block_id,
                  int32_t position, int32_t t, const void* k, const void* v,
                  dd_stream_t stream);
 
+/* Decode-step append of n tokens in one launch (no reference counterpart in
+ * batched form; per token it is ReferenceBackend::append_kv, backend.rs:285-301):
+ * token i of k, v ([n][num_kv_heads][head_dim], src_dtype F32 or BF16) goes
+ * to token slot slots[i] (0..15) of page page_ids[i] (device arrays), in the
+ * pool's storage type: values for F32/BF16 pages (bf16 RNE), RNE-saturating
+ * E4M3 of x / kv_scales[kv][h] for per-head E4M3 pages (the pool's scales
+ * are used as they are), E4M3 codes + E8M0 exponent per 32-element block for
+ * MXFP8 pages (as dd_quantize_kv_pages writes them). Out-of-range page ids or
+ * slots are skipped; if `status` (device, 2 x uint32, may be NULL) is given,
+ * status[0] = 1 and status[1] = the first such token. */
+int dd_append_kv_batch(const dd_attn_config* cfg, void* kv_pages, void* kv_scales, int32_t n,
+                       const uint32_t* page_ids, const int32_t* slots, const void* k,
+                       const void* v, int32_t src_dtype, uint32_t* status, dd_stream_t stream);
+
+/* Copy-on-write data copy: page dst[i] <- page src[i] for i < n (device
+ * arrays; all K/V data of the page and, for MXFP8, its exponent bytes). The
+ * reference's BlockPool::copy_on_write (crates/dendrite-core/src/cache/pool.rs:88-91)
+ * only swaps ids. Invalid ids are skipped (status[0] = 2, status[1] = i). */
+int dd_copy_pages(const dd_attn_config* cfg, void* kv_pages, void* kv_scales, int32_t n,
+                  const uint32_t* src, const uint32_t* dst, uint32_t* status, dd_stream_t stream);
+
 /* KV-page quantization ------------------------------------------------------
  * Replaces QuantizedTensor::quantize / dequantize
  * (crates/dendrite-core/src/quantization/fp8.rs:103-152) with real E4M3 codes.
