@@ -73,7 +73,7 @@ class PlanInfo(C.Structure):
     _fields_ = [("batch_size", C.c_int32), ("num_nodes", C.c_int32), ("num_items", C.c_int32),
                 ("max_depth", C.c_int32), ("kv_tokens", C.c_int64),
                 ("kv_tokens_flat", C.c_int64), ("workspace_bytes", C.c_size_t),
-                ("device_bytes", C.c_size_t), ("kv_tokens_by_kernel", C.c_int64 * 4),
+                ("device_bytes", C.c_size_t), ("kv_tokens_by_kernel", C.c_int64 * 5),
                 ("tc_row_tokens", C.c_int64)]
 
 

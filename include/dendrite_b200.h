@@ -136,8 +136,9 @@ typedef struct dd_plan_info {
   size_t device_bytes;     /* required size of the buffer given to dd_plan_upload */
   /* Unique KV tokens read by each attention kernel: [0] CUDA-core kernel,
    * [1] streaming tensor-core (mma) kernel, [2] tcgen05 kernel (wide nodes),
-   * [3] tcgen05 kernel on CTA pairs (the widest nodes). */
-  int64_t kv_tokens_by_kernel[4];
+   * [3] tcgen05 kernel on CTA pairs (the widest nodes), [4] tcgen05
+   * streaming kernel (narrow nodes, packed). */
+  int64_t kv_tokens_by_kernel[5];
   /* Sum over tcgen05 nodes and KV heads of (query rows x tokens): the
    * kernel's 4 * head_dim FLOPs per unit (Q.K^T and P.V). */
   int64_t tc_row_tokens;
