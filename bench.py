@@ -103,11 +103,18 @@ def make_tree(name: str, rank: int, world: int):
 
 
 class Clocks:
-    """nvidia-smi sampler running during the timed region."""
+    """nvidia-smi sampler (200 ms period) around the timed region. A reader
+    thread collects the samples; `ready()` returns once the first one is in,
+    so the timed steps start with the sampler running, and `stop()` waits for
+    one sample taken after them (a step loop can be shorter than the period)."""
 
     def __init__(self, device_index: int, out: Path | None):
+        import threading
+
         self.proc = None
         self.path = out
+        self.lines: list[str] = []
+        self.t_mark = 0
         q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -117,18 +124,38 @@ class Clocks:
                  "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except (OSError, FileNotFoundError):
             self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            if line.count(",") >= 8:
+                self.lines.append(line.strip())
+
+    def _wait_rows(self, n: int, timeout: float):
+        t0 = time.time()
+        while len(self.lines) < n and time.time() - t0 < timeout and self.proc.poll() is None:
+            time.sleep(0.01)
+
+    def ready(self, timeout: float = 5.0):
+        """Block until the sampler has produced its first sample."""
+        if self.proc:
+            self._wait_rows(1, timeout)
+            self.t_mark = len(self.lines)
 
     def stop(self):
         if not self.proc:
             return None
-        time.sleep(0.25)
+        self._wait_rows(self.t_mark + 1, 2.0)  # a sample taken after the timed steps
         self.proc.terminate()
         try:
-            text, _ = self.proc.communicate(timeout=5)
+            self.proc.wait(timeout=5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
-            text, _ = self.proc.communicate()
-        rows = [r.split(", ") for r in text.strip().splitlines() if r.count(",") >= 8]
+        self.thread.join(timeout=2)
+        text = "\n".join(self.lines) + "\n"
+        rows = [r.split(", ") for r in self.lines]
         if self.path:
             self.path.write_text(text)
         if not rows:
@@ -298,6 +325,7 @@ def timed_steps(step, flush, args, world, rank, local, dev):
     torch.cuda.synchronize()
     clocks = Clocks(local, ROOT / "gpurun_out" / f"clocks_rank{rank}.csv"
                     if (ROOT / "gpurun_out").is_dir() else None)
+    clocks.ready()
     stream = torch.cuda.current_stream()
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
           for _ in range(args.steps)]

@@ -13,9 +13,14 @@
 //    swizzle), plus a bulk copy of the item's query rows into the stream's Q
 //    buffer. Several streams per SM keep enough independent loads in flight
 //    to run HBM near its random-read ceiling.
-//  - FP8 pages land as 1-byte codes (+ E8M0 bytes for MXFP8); the consumer
-//    warp dequantises its stage to bf16 in shared memory (code * scale,
-//    rounded to bf16), so the HBM stream stays 1 byte per element.
+//  - FP8 pages land as 1-byte codes (+ E8M0 bytes for MXFP8) and stay FP8 in
+//    shared memory: the consumer widens them (code * scale rounded to bf16)
+//    straight into its mma fragments. Q.K^T contracts head dims in an order
+//    where a lane's four K codes per k-step are one 4-byte word (Q is loaded
+//    in the same order); for P.V a lane reads one word per token of four
+//    tokens, transposes the 4x4 bytes and widens each head dim's four codes,
+//    and the epilogue puts the head dims back in order. With no bf16 copy of
+//    a stage, the rings hold 5-6 FP8 stages, the same bytes in flight as bf16.
 //  - The consumer warp owns all 16 query rows of its item (a GQA group of one
 //    or more queries sharing the node). Per stage it takes two pages (32
 //    tokens): q.k^T and p.v as m16n8k16 bf16 tensor-core tiles with f32
@@ -45,14 +50,16 @@ struct MmaCfg {
   static constexpr int kSliceBf16 = kPageSize * D * 2;                 // one page, K or V
   static constexpr int kSliceRaw = KV == kKvBf16 ? kSliceBf16 : kPageSize * D;
   static constexpr int kMxBytes = KV == kKvMx ? kPageSize * (D / 32) : 0;
-  static constexpr int kStages = 3;
+  // Stages are read in place by the consumer; FP8 stages are a quarter (E4M3)
+  // of the bf16 ones, so the FP8 rings are deeper for the same bytes in flight.
+  static constexpr int kStages = KV == kKvBf16 ? 3 : 6;
   static constexpr int kRawStage = 2 * kStepPages * kSliceRaw;         // K0 K1 V0 V1
   static constexpr int kMxStage = 2 * kStepPages * kMxBytes;
-  static constexpr int kStageAll = kRawStage + (kMxStage ? ((kMxStage + 1023) / 1024) * 1024 : 0);
-  static constexpr int kConvBytes = KV == kKvBf16 ? 0 : 2 * kStepPages * kSliceBf16;
+  static constexpr int kStageAll = kRawStage;                          // 1 KiB multiple (swizzle)
+  static constexpr int kExpBytes = kStages * kMxStage;                  // MXFP8 exponents, after the stages
   static constexpr int kQRowBytes = D * 2 + 16;                        // padded: conflict-free ldmatrix
   static constexpr int kQBytes = ((kMmaRows * kQRowBytes + 1023) / 1024) * 1024;
-  static constexpr int kStreamBytes = kStages * kStageAll + kConvBytes + kQBytes;
+  static constexpr int kStreamBytes = ((kStages * kStageAll + kExpBytes + kQBytes + 1023) / 1024) * 1024;
   static constexpr int kSmemBytes = kStreams * kStreamBytes + 1024;   // + alignment slack
 };
 
@@ -77,13 +84,14 @@ __device__ __forceinline__ void mma_bf16(float (&c)[4], const uint32_t (&a)[4], 
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-// 3-D TMA load (x, y, z) into shared memory with mbarrier completion.
+// 3-D TMA load (x, y, z) into shared memory with mbarrier completion and an
+// L2 eviction policy.
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int32_t x, int32_t y,
-                                            int32_t z, uint64_t* bar) {
+                                            int32_t z, uint64_t* bar, uint64_t pol) {
   asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
-      "l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3, %4}], [%5], %6;" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar)), "l"(pol)
       : "memory");
 }
 
@@ -93,6 +101,11 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, i
 __device__ __forceinline__ uint32_t swz_bf16(int t, int chunk) {
   return (uint32_t)((chunk >> 3) * 2048 + t * 128 + (((chunk & 7) ^ (t & 7)) << 4));
 }
+
+// FP8 QK^T k order: k-step kk of lane c covers head dims fp8_kdim(kk, c) + 0..3
+// (16-byte chunk c for k-steps 0-3, chunk c + 4 for 4-7), so the lane's four
+// K codes of one token per k-step are one aligned 4-byte word.
+__device__ __forceinline__ int fp8_kdim(int kk, int c) { return 16 * (c + 4 * (kk >> 2)) + 4 * (kk & 3); }
 
 struct StageMeta {
   int8_t item_slot;
@@ -115,11 +128,12 @@ enum { kFirst = 1, kLast = 2, kDone = 4 };
 #define DD_TFLUSH(a, slot, acc)
 #endif
 
+constexpr int kMaxStages = 6;
 struct StreamShared {
-  uint64_t full[3];
-  uint64_t empty[3];
+  uint64_t full[kMaxStages];
+  uint64_t empty[kMaxStages];
   uint64_t q_empty;
-  StageMeta meta[3];
+  StageMeta meta[kMaxStages];
   WorkItem items[kItemSlots];
 };
 
@@ -127,6 +141,7 @@ template <int D, int KV>
 __global__ void __launch_bounds__(kMmaThreads, 1)
     attn_mma_kernel(const __grid_constant__ CUtensorMap kv_map, AttnArgs a) {
   using C = MmaCfg<D, KV>;
+  static_assert(KV == kKvBf16 || D == 128, "FP8 fragments are laid out for head_dim 128");
   constexpr int S = C::kStages;
   extern __shared__ uint8_t smem_raw[];
   __shared__ StreamShared ss[kStreams];
@@ -159,7 +174,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
     const int c = warp - kStreams;
     StreamShared& sh = ss[c];
     uint8_t* base = smem + c * C::kStreamBytes;
-    uint8_t* qbuf = base + S * C::kStageAll + C::kConvBytes;
+    uint8_t* qbuf = base + S * C::kStageAll + C::kExpBytes;
     int stage_idx = 0, item_count = 0;
     bool need_item = true, finished = false;
     WorkItem it{};
@@ -176,6 +191,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
     int pf_state = 0, pf_idx = 0;
     uint32_t pf_claim = 0;             // lane 0: claimed item index, in flight
     WorkItem pf_it{};
+    bool pf_sole = false;              // the item is the only reader of its pages
     const uint32_t* pf_pages = nullptr;
     uint32_t pf_id = 0, pf_id2 = 0;
     int pf_qid = 0;                    // lane r < nrows: query index of row r
@@ -184,7 +200,11 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
         if (lane == 0) pf_claim = atomicAdd(&a.err->work_counter, 1u);
       } else if (pf_state == 1) {
         pf_idx = (int)__shfl_sync(0xffffffffu, pf_claim, 0);
-        if (pf_idx < a.num_items) pf_it = resolve_item_idx(a, pf_idx, pf_pages, kMmaRows);
+        if (pf_idx < a.num_items) {
+          pf_it = resolve_item_idx(a, pf_idx, pf_pages, kMmaRows);
+          pf_sole = a.items ? (pf_it.nrows & kItemSoleReader) != 0 : a.row_tiles == 1;
+          pf_it.nrows &= kItemRowsMask;
+        }
       } else if (pf_state == 2) {
         if (pf_idx < a.num_items) {
           pf_id = lane < pf_it.npages ? pf_pages[lane] : 0u;
@@ -198,6 +218,8 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
       }
       ++pf_state;
     };
+    const uint64_t pol_first = l2_policy(true), pol_normal = l2_policy(false);
+    uint64_t pol = pol_normal;
     long long t_pf = 0, t_empty = 0, t_qe = 0;
     DD_TSTART(tlife)
     uint64_t t_idle = global_ns();
@@ -211,6 +233,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
         done = pf_idx >= a.num_items;
         if (!done) {
           it = pf_it;
+          pol = pf_sole ? pol_first : pol_normal;
           pages = pf_pages;
           pi = 0;
           chunk_base = 0;
@@ -309,13 +332,13 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
           uint8_t* st = base + s * C::kStageAll;
           uint8_t* dst = st + (kv * kStepPages + j) * C::kSliceRaw;
           if (KV == kKvBf16 && D == 128)
-            tma_load_3d(dst, &kv_map, 0, y, 0, &sh.full[s]);
+            tma_load_3d(dst, &kv_map, 0, y, 0, &sh.full[s], pol);
           else
-            tma_load_2d(dst, &kv_map, 0, y, &sh.full[s]);
+            tma_load_2d_hint(dst, &kv_map, 0, y, &sh.full[s], pol);
           if (KV == kKvMx)
-            bulk_load(st + C::kRawStage + (kv * kStepPages + j) * C::kMxBytes,
-                      reinterpret_cast<const uint8_t*>(a.scales) + (size_t)y * (D / 32),
-                      C::kMxBytes, &sh.full[s]);
+            bulk_load_hint(base + S * C::kStageAll + s * C::kMxStage + (kv * kStepPages + j) * C::kMxBytes,
+                           reinterpret_cast<const uint8_t*>(a.scales) + (size_t)y * (D / 32),
+                           C::kMxBytes, &sh.full[s], pol);
         }
         pi += np;
         if (pi - chunk_base >= 32) {
@@ -349,13 +372,12 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
     // ------------------------------------------------------------ consumer
     StreamShared& sh = ss[warp];
     uint8_t* base = smem + warp * C::kStreamBytes;
-    uint8_t* conv = base + S * C::kStageAll;
-    uint8_t* qbuf = conv + C::kConvBytes;
+    uint8_t* qbuf = base + S * C::kStageAll + C::kExpBytes;
     WorkItem it{};
     uint32_t qa[D / 16][4];
     float o[D / 8][4];
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
-    float sc_k = 1.f, sc_v = 1.f;
+    float sc_k = 1.f, sc_v = 1.f;  // per-head E4M3 scales of the current item
     int items_started = 0;
     long long t_full = 0;
     DD_TSTART(tclife)
@@ -370,12 +392,28 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
       if (m.flags & kDone) break;
       if (m.flags & kFirst) {
         it = sh.items[m.item_slot];
-        const uint32_t qbase = smem_u32(qbuf);
+        if (KV == kKvBf16) {
+          const uint32_t qbase = smem_u32(qbuf);
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const int row = (lane & 7) + (((lane >> 3) & 1) << 3);
-          const int chunk = kk * 2 + (lane >> 4);
-          ldsm_x4(qbase + row * C::kQRowBytes + chunk * 16, qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3]);
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const int row = (lane & 7) + (((lane >> 3) & 1) << 3);
+            const int chunk = kk * 2 + (lane >> 4);
+            ldsm_x4(qbase + row * C::kQRowBytes + chunk * 16, qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3]);
+          }
+        } else {
+          // FP8: k-step kk, k = 2c..2c+1 / 2c+8..2c+9 of lane c = lane % 4 is
+          // head dim fp8_kdim(kk, c) + 0..1 / + 2..3, the order in which the
+          // lane finds the codes of one token in one 4-byte word.
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const int pd = fp8_kdim(kk, lane & 3);
+            const uint2 r0 = *reinterpret_cast<const uint2*>(qbuf + (lane >> 2) * C::kQRowBytes + pd * 2);
+            const uint2 r1 = *reinterpret_cast<const uint2*>(qbuf + ((lane >> 2) + 8) * C::kQRowBytes + pd * 2);
+            qa[kk][0] = r0.x;
+            qa[kk][1] = r1.x;
+            qa[kk][2] = r0.y;
+            qa[kk][3] = r1.y;
+          }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&sh.q_empty);
@@ -393,36 +431,8 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
       const uint8_t* st = base + s * C::kStageAll;
       const uint8_t* kb;
       const uint8_t* vb;
-      if (KV == kKvBf16) {
-        kb = st;
-        vb = st + kStepPages * C::kSliceRaw;
-      } else {
-        // Widen the stage's codes into the warp's bf16 buffer: per page
-        // slice 16 tokens x D/16 chunks of 16 codes, lane-strided.
-        for (int kv = 0; kv < 2; ++kv)
-          for (int j = 0; j < np; ++j) {
-            const uint8_t* src = st + (kv * kStepPages + j) * C::kSliceRaw;
-            const uint8_t* mx = st + C::kRawStage + (kv * kStepPages + j) * C::kMxBytes;
-            uint8_t* dst = conv + (kv * kStepPages + j) * C::kSliceBf16;
-#pragma unroll
-            for (int i = 0; i < kPageSize * (D / 16) / 32; ++i) {
-              const int u = lane + 32 * i;
-              const int c = u % (D / 16), t = u / (D / 16);  // 16-code chunk along D, token
-              const uint4 codes =
-                  *reinterpret_cast<const uint4*>(src + t * D + (((c & 7) ^ (t & 7)) << 4));
-              // Per-head E4M3 scales are applied to the scores and the output.
-              const float mul = KV == kKvMx ? e8m0_to_float(mx[t * (D / 32) + (c >> 1)]) : (kv ? sc_v : sc_k);
-              uint32_t w[8];
-              e4m3x16_to_bf16(codes, mul, w);
-              *reinterpret_cast<uint4*>(dst + swz_bf16(t, 2 * c)) = make_uint4(w[0], w[1], w[2], w[3]);
-              *reinterpret_cast<uint4*>(dst + swz_bf16(t, 2 * c + 1)) = make_uint4(w[4], w[5], w[6], w[7]);
-            }
-          }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&sh.empty[s]);  // raw stage may be refilled
-        kb = conv;
-        vb = conv + kStepPages * C::kSliceBf16;
-      }
+      kb = st;
+      vb = st + kStepPages * C::kSliceRaw;
       // Valid tokens per page of the step (0 = absent or skipped).
       int valid[2];
 #pragma unroll
@@ -433,25 +443,77 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
         valid[j] = 0;  // data-movement ceiling experiment only
 #endif
       }
+      // MXFP8 exponent words of the stage, read before any code is widened:
+      // kex[nt] = the four 32-dim blocks of K token nt*8 + lane/4, vex[j][i]
+      // = those of V token 2c, 2c+1, 2c+8, 2c+9 (c = lane % 4) of page j.
+      uint32_t kex[4] = {0u, 0u, 0u, 0u}, vex[2][4] = {{0u, 0u, 0u, 0u}, {0u, 0u, 0u, 0u}};
+      if (KV == kKvMx) {
+        const uint8_t* mx = base + S * C::kStageAll + s * C::kMxStage;
+#pragma unroll
+        for (int nt = 0; nt < 4; ++nt)
+          kex[nt] = *reinterpret_cast<const uint32_t*>(mx + (nt >> 1) * C::kMxBytes +
+                                                        ((nt & 1) * 8 + (lane >> 2)) * (D / 32));
+#pragma unroll
+        for (int j = 0; j < 2; ++j)
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            vex[j][i] = *reinterpret_cast<const uint32_t*>(
+                mx + (kStepPages + j) * C::kMxBytes + (2 * (lane & 3) + (i & 1) + 8 * (i >> 1)) * (D / 32));
+      }
       if (valid[0] + valid[1] > 0) {
         // S = Q K^T for 16 rows x 32 tokens: four independent n-tile chains.
         float sacc[4][4];
 #pragma unroll
         for (int nt = 0; nt < 4; ++nt) sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.f;
-        const uint32_t k0 = smem_u32(kb), k1 = smem_u32(kb + C::kSliceBf16);
         const bool two = valid[1] > 0;
+        if (KV == kKvBf16) {
+          const uint32_t k0 = smem_u32(kb), k1 = smem_u32(kb + C::kSliceBf16);
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const int t = ((lane >> 4) << 3) + (lane & 7);
-          const int chunk = kk * 2 + ((lane >> 3) & 1);
-          uint32_t b0, b1, b2, b3;
-          ldsm_x4(k0 + swz_bf16(t, chunk), b0, b1, b2, b3);
-          mma_bf16(sacc[0], qa[kk], b0, b1);
-          mma_bf16(sacc[1], qa[kk], b2, b3);
-          if (two) {
-            ldsm_x4(k1 + swz_bf16(t, chunk), b0, b1, b2, b3);
-            mma_bf16(sacc[2], qa[kk], b0, b1);
-            mma_bf16(sacc[3], qa[kk], b2, b3);
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const int t = ((lane >> 4) << 3) + (lane & 7);
+            const int chunk = kk * 2 + ((lane >> 3) & 1);
+            uint32_t b0, b1, b2, b3;
+            ldsm_x4(k0 + swz_bf16(t, chunk), b0, b1, b2, b3);
+            mma_bf16(sacc[0], qa[kk], b0, b1);
+            mma_bf16(sacc[1], qa[kk], b2, b3);
+            if (two) {
+              ldsm_x4(k1 + swz_bf16(t, chunk), b0, b1, b2, b3);
+              mma_bf16(sacc[2], qa[kk], b0, b1);
+              mma_bf16(sacc[3], qa[kk], b2, b3);
+            }
+          }
+        } else {
+          // FP8 K straight from the stage: n-tile nt is tokens nt*8..+7; lane
+          // (g, c) = (lane / 4, lane % 4) widens token nt*8 + g's codes of
+          // 16-byte chunks c and c + 4 (k-steps 0-3 and 4-7) into the B
+          // fragments. Odd tokens load chunk c + 4 first, so each 8-lane
+          // phase of the 16-byte loads covers all 32 banks.
+          const int c = lane & 3;
+          uint4 kx[4], ky[4];
+#pragma unroll
+          for (int nt = 0; nt < 4; ++nt) {
+            const int tp = (nt & 1) * 8 + (lane >> 2), odd = tp & 1;
+            const uint8_t* row = kb + (nt >> 1) * C::kSliceRaw + tp * D;
+            kx[nt] = *reinterpret_cast<const uint4*>(row + (((c + 4 * odd) ^ (tp & 7)) << 4));
+            ky[nt] = *reinterpret_cast<const uint4*>(row + (((c + 4 - 4 * odd) ^ (tp & 7)) << 4));
+          }
+#pragma unroll
+          for (int nt = 0; nt < 4; ++nt) {
+            if (nt >= 2 && !two) break;
+            const int odd = ((lane >> 2) & 1);
+            const uint4 lo = odd ? ky[nt] : kx[nt], hi = odd ? kx[nt] : ky[nt];
+            float mlo = sc_k, mhi = sc_k;
+            if (KV == kKvMx) {
+              mlo = e8m0_byte_to_float(kex[nt], c >> 1);
+              mhi = e8m0_byte_to_float(kex[nt], 2 + (c >> 1));
+            }
+            const uint32_t wv[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk) {
+              uint32_t b0, b1;
+              e4m3x4_to_bf16_cvt(wv[kk], kk < 4 ? mlo : mhi, b0, b1);
+              mma_bf16(sacc[nt], qa[kk], b0, b1);
+            }
           }
         }
         // x[nt][0..1]: row lane/4, tokens nt*8+tc+{0,1}; x[nt][2..3]: row +8.
@@ -507,24 +569,57 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
           split_bf16x2(p[2 * j][2], p[2 * j][3], pa[1], pl[1]);
           split_bf16x2(p[2 * j + 1][0], p[2 * j + 1][1], pa[2], pl[2]);
           split_bf16x2(p[2 * j + 1][2], p[2 * j + 1][3], pa[3], pl[3]);
-          const uint32_t vaddr = smem_u32(vb + j * C::kSliceBf16);
+          if (KV == kKvBf16) {
+            const uint32_t vaddr = smem_u32(vb + j * C::kSliceBf16);
 #pragma unroll
-          for (int nn = 0; nn < D / 16; ++nn) {
-            const int t = (((lane >> 3) & 1) << 3) + (lane & 7);
-            const int chunk = nn * 2 + (lane >> 4);
-            uint32_t b0, b1, b2, b3;
-            ldsm_x4_t(vaddr + swz_bf16(t, chunk), b0, b1, b2, b3);
-            mma_bf16(o[2 * nn], pa, b0, b1);
-            mma_bf16(o[2 * nn + 1], pa, b2, b3);
-            mma_bf16(o[2 * nn], pl, b0, b1);
-            mma_bf16(o[2 * nn + 1], pl, b2, b3);
+            for (int nn = 0; nn < D / 16; ++nn) {
+              const int t = (((lane >> 3) & 1) << 3) + (lane & 7);
+              const int chunk = nn * 2 + (lane >> 4);
+              uint32_t b0, b1, b2, b3;
+              ldsm_x4_t(vaddr + swz_bf16(t, chunk), b0, b1, b2, b3);
+              mma_bf16(o[2 * nn], pa, b0, b1);
+              mma_bf16(o[2 * nn + 1], pa, b2, b3);
+              mma_bf16(o[2 * nn], pl, b0, b1);
+              mma_bf16(o[2 * nn + 1], pl, b2, b3);
+            }
+          } else {
+            // FP8 V straight from the stage: lane (g, c) reads, per 32-dim
+            // block b, dims 32b + 4g .. +3 of tokens 2c, 2c+1, 2c+8, 2c+9 (one
+            // word each), transposes the 4x4 bytes, and widens dim d's four
+            // codes into the B fragment of n-tile 4b + d, whose column g is
+            // head dim 32b + 4g + d (fp8_odim).
+            const uint8_t* vs = vb + j * C::kSliceRaw;
+            const int g = lane >> 2, c = lane & 3;
+            const int t0 = 2 * c, t1 = 2 * c + 1, t2 = 2 * c + 8, t3 = 2 * c + 9;
+#pragma unroll
+            for (int b = 0; b < D / 32; ++b) {
+              const int off = 4 * (g & 3);
+              const int ch = 2 * b + (g >> 2);
+              const uint32_t w0 = *reinterpret_cast<const uint32_t*>(vs + t0 * D + ((ch ^ (t0 & 7)) << 4) + off);
+              const uint32_t w1 = *reinterpret_cast<const uint32_t*>(vs + t1 * D + ((ch ^ (t1 & 7)) << 4) + off);
+              const uint32_t w2 = *reinterpret_cast<const uint32_t*>(vs + t2 * D + ((ch ^ (t2 & 7)) << 4) + off);
+              const uint32_t w3 = *reinterpret_cast<const uint32_t*>(vs + t3 * D + ((ch ^ (t3 & 7)) << 4) + off);
+              const uint32_t a01 = __byte_perm(w0, w1, 0x5140), b01 = __byte_perm(w0, w1, 0x7362);
+              const uint32_t a23 = __byte_perm(w2, w3, 0x5140), b23 = __byte_perm(w2, w3, 0x7362);
+              const uint32_t u[4] = {__byte_perm(a01, a23, 0x5410), __byte_perm(a01, a23, 0x7632),
+                                     __byte_perm(b01, b23, 0x5410), __byte_perm(b01, b23, 0x7632)};
+              float m4[4];
+#pragma unroll
+              for (int i = 0; i < 4; ++i)
+                m4[i] = KV == kKvMx ? e8m0_byte_to_float(vex[j][i], b) : sc_v;
+#pragma unroll
+              for (int d = 0; d < 4; ++d) {
+                uint32_t b0, b1;
+                e4m3x4_to_bf16_mul4(u[d], m4, b0, b1);
+                mma_bf16(o[4 * b + d], pa, b0, b1);
+                mma_bf16(o[4 * b + d], pl, b0, b1);
+              }
+            }
           }
         }
       }
-      if (KV == kKvBf16) {
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&sh.empty[s]);
-      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sh.empty[s]);
       if (m.flags & kLast) {
         // Normalised partial state per row, written from registers.
         float L0 = l0 + __shfl_xor_sync(0xffffffffu, l0, 1);
@@ -540,11 +635,23 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
           const int rr = it.row0 + r, qi = rr / a.g;
           const int hq = qo_head_of(a.gqa_map, it.kv_head, rr % a.g, a.Hkv, a.g);
           const int64_t slot = (int64_t)it.slot_base + (int64_t)qi * a.Hq + hq;
-          float* dst = a.part_o + slot * D + tc;
+          if (KV == kKvBf16) {
+            float* dst = a.part_o + slot * D + tc;
 #pragma unroll
-          for (int n = 0; n < D / 8; ++n)
-            *reinterpret_cast<float2*>(dst + n * 8) =
-                make_float2(o[n][2 * half] * inv, o[n][2 * half + 1] * inv);
+            for (int n = 0; n < D / 8; ++n)
+              *reinterpret_cast<float2*>(dst + n * 8) =
+                  make_float2(o[n][2 * half] * inv, o[n][2 * half + 1] * inv);
+          } else {
+            // n-tile 4b + d, column 2c + e is head dim 32b + 8c + 4e + d.
+            float* dst = a.part_o + slot * D + 8 * (lane & 3);
+#pragma unroll
+            for (int b = 0; b < D / 32; ++b)
+#pragma unroll
+              for (int e = 0; e < 2; ++e)
+                *reinterpret_cast<float4*>(dst + 32 * b + 4 * e) =
+                    make_float4(o[4 * b][2 * half + e] * inv, o[4 * b + 1][2 * half + e] * inv,
+                                o[4 * b + 2][2 * half + e] * inv, o[4 * b + 3][2 * half + e] * inv);
+          }
           if ((lane & 3) == 0) a.part_lse[slot] = L > 0.f ? M + log2f(L) : -INFINITY;
         }
       }

@@ -56,43 +56,20 @@ __device__ __forceinline__ uint8_t float_to_e4m3_satrn(float x) {
 
 // E8M0 shared exponent byte -> 2^(c-127) as f32 (c = 0 gives 2^-127, a
 // subnormal f32; c = 255 is NaN in the format and is never produced).
-__device__ __forceinline__ float e8m0_to_float(uint8_t c) {
-  if (c == 0) return __uint_as_float(0x00400000u);  // 2^-127
-  if (c == 255) return __uint_as_float(0x7fc00000u);
-  return __uint_as_float((uint32_t)c << 23);
+// Branch-free: y = c << 23; c = 0 gives max(0, 2^-127 bits), c = 255 gives
+// 0x7f800000, to which the carry out of y + 2^23 adds the quiet-NaN bit.
+__device__ __forceinline__ float e8m0_bits_to_float(uint32_t y) {
+  return __uint_as_float(max(y, 0x00400000u) | (((y + 0x00800000u) >> 9) & 0x00400000u));
+}
+__device__ __forceinline__ float e8m0_to_float(uint8_t c) { return e8m0_bits_to_float((uint32_t)c << 23); }
+// The same for the E8M0 byte `b` (0-3) of a word.
+__device__ __forceinline__ float e8m0_byte_to_float(uint32_t w, uint32_t b) {
+  return e8m0_bits_to_float(__byte_perm(w, 0u, 0x0444u | (b << 12)) >> 1);
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
-}
-
-// 16 E4M3 codes -> 16 bf16 = code * mul (f32 product, rounded once to bf16;
-// exact for E4M3 times a power of two in bf16's normal range). The hardware
-// E4M3 -> f16 conversion keeps NaN codes NaN. An integer-only variant (codes
-// placed into bf16 bits, then one bf16 multiply) measured slower on B200.
-__device__ __forceinline__ void e4m3x16_to_bf16(const uint4 c, float mul, uint32_t (&r)[8]) {
-  const uint32_t w[4] = {c.x, c.y, c.z, c.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float2 a = e4m3x2_to_float2((uint16_t)(w[i] & 0xffffu));
-    const float2 b = e4m3x2_to_float2((uint16_t)(w[i] >> 16));
-    r[2 * i] = pack_bf16x2(a.x * mul, a.y * mul);
-    r[2 * i + 1] = pack_bf16x2(b.x * mul, b.y * mul);
-  }
-}
-
-// Two-term bf16 split of a pair of non-negative finite floats (softmax
-// probabilities): x = hi + lo + e with hi = x truncated to bf16, lo = (x - hi)
-// truncated to bf16 (x - hi is exact in f32). |e| < 2^-14 |x|. Only integer
-// and f32 add units are used (no conversion instructions), so the split costs
-// nothing on the pipe that also evaluates the exponentials.
-__device__ __forceinline__ void split_bf16x2(float a, float b, uint32_t& hi, uint32_t& lo) {
-  const uint32_t ua = __float_as_uint(a), ub = __float_as_uint(b);
-  hi = __byte_perm(ua, ub, 0x7632);  // high halves: a in the low 16 bits
-  const float ra = a - __uint_as_float(ua & 0xffff0000u);
-  const float rb = b - __uint_as_float(ub & 0xffff0000u);
-  lo = __byte_perm(__float_as_uint(ra), __float_as_uint(rb), 0x7632);
 }
 
 // Packed pair arithmetic (sm_100 f32x2 instructions: two lanes of f32 per
@@ -121,6 +98,56 @@ __device__ __forceinline__ float max3f(float a, float b, float c) {
   float d;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
   return d;
+}
+
+// 16 E4M3 codes -> 16 bf16 = code * mul (f32 product, rounded once to bf16;
+// exact for E4M3 times a power of two in bf16's normal range). The hardware
+// E4M3 -> f16 conversion keeps NaN codes NaN. An integer-only variant (codes
+// placed into bf16 bits, then one bf16 multiply) measured slower on B200.
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+// Four E4M3 codes (bytes 0-3 of w) times mul to two bf16x2 words (bytes 0-1
+// -> r0, 2-3 -> r1): hardware E4M3 -> f16 -> f32, one packed f32 product per
+// pair, round to nearest even to bf16.
+__device__ __forceinline__ void e4m3x4_to_bf16_cvt(uint32_t w, float mul, uint32_t& r0, uint32_t& r1) {
+  const float2 a = e4m3x2_to_float2((uint16_t)(w & 0xffffu));
+  const float2 b = e4m3x2_to_float2((uint16_t)(w >> 16));
+  const uint64_t m2 = f2_pack(mul, mul);
+  const uint64_t pa = f2_mul(f2_pack(a.x, a.y), m2), pb = f2_mul(f2_pack(b.x, b.y), m2);
+  r0 = pack_bf16x2(f2_lo(pa), f2_hi(pa));
+  r1 = pack_bf16x2(f2_lo(pb), f2_hi(pb));
+}
+// Four E4M3 codes (bytes 0-3 of w), each with its own multiplier, to two
+// bf16x2 words (bytes 0-1 -> r0, 2-3 -> r1); same rounding as above.
+__device__ __forceinline__ void e4m3x4_to_bf16_mul4(uint32_t w, const float (&m)[4], uint32_t& r0,
+                                                    uint32_t& r1) {
+  const float2 a = e4m3x2_to_float2((uint16_t)(w & 0xffffu));
+  const float2 b = e4m3x2_to_float2((uint16_t)(w >> 16));
+  const uint64_t pa = f2_mul(f2_pack(a.x, a.y), f2_pack(m[0], m[1]));
+  const uint64_t pb = f2_mul(f2_pack(b.x, b.y), f2_pack(m[2], m[3]));
+  r0 = pack_bf16x2(f2_lo(pa), f2_hi(pa));
+  r1 = pack_bf16x2(f2_lo(pb), f2_hi(pb));
+}
+__device__ __forceinline__ void e4m3x16_to_bf16(const uint4 c, float mul, uint32_t (&r)[8]) {
+  const uint32_t w[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) e4m3x4_to_bf16_cvt(w[i], mul, r[2 * i], r[2 * i + 1]);
+}
+
+// Two-term bf16 split of a pair of non-negative finite floats (softmax
+// probabilities): x = hi + lo + e with hi = x truncated to bf16, lo = (x - hi)
+// truncated to bf16 (x - hi is exact in f32). |e| < 2^-14 |x|. Only integer
+// and f32 add units are used (no conversion instructions), so the split costs
+// nothing on the pipe that also evaluates the exponentials.
+__device__ __forceinline__ void split_bf16x2(float a, float b, uint32_t& hi, uint32_t& lo) {
+  const uint32_t ua = __float_as_uint(a), ub = __float_as_uint(b);
+  hi = __byte_perm(ua, ub, 0x7632);  // high halves: a in the low 16 bits
+  const float ra = a - __uint_as_float(ua & 0xffff0000u);
+  const float rb = b - __uint_as_float(ub & 0xffff0000u);
+  lo = __byte_perm(__float_as_uint(ra), __float_as_uint(rb), 0x7632);
 }
 
 // split_bf16x2 with the two subtractions as one packed instruction.
@@ -209,6 +236,35 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
       "l"(src), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
+// The same two copies with an L2 cache-eviction policy (from l2_policy).
+__device__ __forceinline__ void tma_load_2d_hint(void* dst, const CUtensorMap* map, int32_t x,
+                                                 int32_t y, uint64_t* bar, uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(pol)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_load_hint(void* dst, const void* src, uint32_t bytes,
+                                               uint64_t* bar, uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1], %2, [%3], %4;" ::"r"(smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
+      : "memory");
+}
+// L2 policies: evict_first for data this CTA alone reads once (a streamed
+// leaf's pages), so it does not push out what other CTAs or the next kernel
+// re-read (shared prefix pages, partial states); evict_normal otherwise.
+__device__ __forceinline__ uint64_t l2_policy(bool evict_first) {
+  uint64_t pol;
+  if (evict_first)
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  else
+    asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
 }
@@ -289,7 +345,7 @@ __device__ __forceinline__ WorkItem resolve_item_idx(const AttnArgs& a, int idx,
   if (a.items) {
     it = a.items[idx];
     pages = a.pages + it.page_off;
-    return it;
+    return it;  // nrows may carry kItemSoleReader: callers mask with kItemRowsMask
   }
   const int s = idx % a.nsplit;
   const int rest = idx / a.nsplit;

@@ -42,6 +42,11 @@ struct WorkItem {
   int32_t slot_base;   // partial-state slot of (node, chunk, query 0, head 0)
 };
 static_assert(sizeof(WorkItem) == 32, "WorkItem layout");
+// Streaming (kItemMma) items: nrows bit 16 marks an item that is the only
+// reader of its pages in the launch (its node has one row tile), which then
+// streams them with an L2 evict-first policy.
+constexpr int32_t kItemSoleReader = 1 << 16;
+constexpr int32_t kItemRowsMask = 0xffff;
 
 // Device-side view of an uploaded plan (pointers into the caller's buffer).
 struct DevicePlan {

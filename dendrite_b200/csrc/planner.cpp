@@ -412,6 +412,7 @@ static void build_items(dd_plan* p) {
           it.kv_head = h;
           it.row0 = (int32_t)(t * rt);
           it.nrows = (int32_t)std::min<int64_t>(rt, rows - t * rt);
+          if (kind == kItemMma && row_tiles == 1) it.nrows |= kItemSoleReader;
           it.q_begin = n.q_begin;
           it.slot_base = slot_base;
           p->items[kind].push_back(it);
