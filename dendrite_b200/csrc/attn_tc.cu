@@ -52,7 +52,11 @@ constexpr int kTcStageBytes = kTcStageCodes + kTcStageExps;
 
 // Per KV dtype: bf16 pages are copied by TMA straight into the bf16 K/V ring;
 // FP8 pages (E4M3 codes) are copied into a staging ring and two converter
-// warps (10-11) widen them to bf16 in the ring's swizzled layout.
+// warps (10-13) widen them to bf16 in the ring's swizzled layout.
+// FP8 converter warps (10-13). Four keep the widening ahead of the tensor
+// pipe (two left the MXFP8 root ~25% slower); at 448 threads the kernel is
+// held to 128 registers and spills ~90 bytes outside the inner loops.
+constexpr int kTcConvWarps = 4;
 template <int KV>
 struct TcCfg {
   static constexpr bool kFp8 = KV != DD_DTYPE_BF16;
@@ -61,7 +65,7 @@ struct TcCfg {
 #else
   static constexpr int kSlots = kFp8 ? 3 : 4;    // K/V ring slots (32 KiB each)
 #endif
-  static constexpr int kThreads = kFp8 ? 384 : 320;
+  static constexpr int kThreads = kFp8 ? 320 + 32 * kTcConvWarps : 320;
   static constexpr int kSmem =
       2 * kTcQBytes + kSlots * kTcSlotBytes + (kFp8 ? kTcStages * kTcStageBytes : 0) + 1024;
 };
@@ -119,12 +123,12 @@ __global__ void __launch_bounds__(TcCfg<KV>::kThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kTcSlots; ++s) {
-      mbar_init(&bars.kv_full[s], kFp8 ? 64 : 1);
+      mbar_init(&bars.kv_full[s], kFp8 ? 32 * kTcConvWarps : 1);
       mbar_init(&bars.kv_empty[s], 1);
     }
     for (int s = 0; s < kTcStages; ++s) {
       mbar_init(&bars.st_full[s], 1);
-      mbar_init(&bars.st_empty[s], 64);
+      mbar_init(&bars.st_empty[s], 32 * kTcConvWarps);
     }
     for (int x = 0; x < 2; ++x) {
       mbar_init(&bars.s_full[x], 1);
@@ -294,11 +298,12 @@ __global__ void __launch_bounds__(TcCfg<KV>::kThreads, 1)
     }
   } else if (kFp8 && warp >= 10) {
     // ----------------------------------------------------------- converters
-    // Thread t of 64 widens chunks id = i*64 + t (i < 16) of each staged tile:
+    // Thread t of 128 widens chunks id = t + 128 i (i < 8) of each staged tile:
     // chunk = 16 codes of one token (row), dims 16c..16c+15. Consecutive
     // threads cover two rows x four chunks of one dim-half, so each quarter
     // warp's two 16-byte stores hit eight distinct bank groups.
     const int t = threadIdx.x - 320;
+    constexpr int kConvThreads = 32 * kTcConvWarps;
     for (int idx = 0; idx < 2 * ntiles; ++idx) {
       const int su = idx % kTcStages, s = idx % kTcSlots;
       if (!mbar_wait(&bars.st_full[su], (idx / kTcStages) & 1, abort, a.err)) break;
@@ -313,8 +318,7 @@ __global__ void __launch_bounds__(TcCfg<KV>::kThreads, 1)
       // Rows of absent pages hold zero codes but no exponents.
       const int live_rows = kPageSize * min(kTcPagesPerTile, npages - (idx >> 1) * kTcPagesPerTile);
 #pragma unroll 4
-      for (int i = 0; i < 16; ++i) {
-        const int id = i * 64 + t;
+      for (int id = t; id < 1024; id += kConvThreads) {
         const int cl = id & 3, half = (id >> 3) & 1;
         const int row = ((id >> 4) << 1) | ((id >> 2) & 1);
         const int c = half * 4 + cl;
