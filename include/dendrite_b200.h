@@ -37,6 +37,11 @@
  *                      uint8 E8M0 [num_pages][2][num_kv_heads][16][head_dim/32]
  *                      (one shared exponent per 32 consecutive elements of a
  *                      token's head vector, OCP MX v1.0).
+ *    Slots of a sequence's last page beyond its valid tokens must hold finite
+ *    values (their scores are masked, but the kernels multiply their zero
+ *    weights by the stored V); Dendrite's pages start zeroed
+ *    (Tensor::zeros, cache/paged.rs:86-92) and the quantize / append entry
+ *    points here write only finite codes.
  *  - Queries / outputs: [batch][num_qo_heads][head_dim] (q_dtype, out in
  *    q_dtype). lse: float [batch][num_qo_heads], natural-log log-sum-exp of
  *    the scaled scores, the convention of merge_attention_outputs
