@@ -61,6 +61,9 @@ WORKLOADS = {
     "long70b": dict(kind="tree", kv="bf16", tree="long", split="kv-heads",
                     desc="config 5b: Llama-3-70B heads, one tree 131072 prefix + 256 x 256, "
                          "KV-head split + all-gather"),
+    "prefill8b": dict(kind="tree", kv="bf16", tree="prefill", split="trees-per-rank",
+                      desc="chunked prefill of branch suffixes: Llama-3-8B heads, 8192-token shared "
+                           "prefix, 16 branches x 64 new tokens (queries = new tokens)"),
     "quant-e4m3": dict(kind="quant", fmt="e4m3",
                        desc="config 2: per-head E4M3 quantize of 4096 x [2][4][16][64] bf16 pages"),
     "quant-mxfp8": dict(kind="quant", fmt="mxfp8",
@@ -90,6 +93,10 @@ def make_tree(name: str, rank: int, world: int):
     from dendrite_b200 import workloads as wl
 
     w = WORKLOADS[name]
+    if w["tree"] == "prefill":
+        # one new token = one query over its sequence's first prefix + i + 1 tokens
+        tb = wl.prefill_branches_8b(SEED + rank).nested()
+        return tb, tb.batch_size * world
     if w["tree"] == "mcts":
         tb = wl.mcts_llama3_8b(SEED + rank)
         return tb, tb.batch_size * world
@@ -389,6 +396,7 @@ def run_tree(args, world, rank, local, dev):
     import dendrite_b200 as dd
     from dendrite_b200 import _lib
     from dendrite_b200 import head_split as hs
+    from dendrite_b200 import workloads as wl
 
     w = WORKLOADS[args.workload]
     kv = w["kv"]
@@ -421,7 +429,14 @@ def run_tree(args, world, rank, local, dev):
         del pool
     else:
         lcfg, kv_local, sc_local, q_local = cfg, kv_pages, scales, q
-    plan = dd.CascadePlan(lcfg, tb.indptr, tb.block_ids, tb.num_tokens)
+    pb = wl.prefill_branches_8b(SEED + rank) if w["tree"] == "prefill" else None
+
+    def make_plan():
+        if pb is not None:
+            return dd.CascadePlan.prefill(lcfg, pb.indptr, pb.block_ids, pb.prefix_len, pb.num_new)
+        return dd.CascadePlan(lcfg, tb.indptr, tb.block_ids, tb.num_tokens)
+
+    plan = make_plan()
     plan.upload(dev)
     info = plan.info()
     ws = torch.empty(max(int(info.workspace_bytes), 256), dtype=torch.uint8, device=dev)
@@ -486,13 +501,20 @@ def run_tree(args, world, rank, local, dev):
     res = out if heads else out_local
     out_host = torch.empty(res.shape, dtype=res.dtype).pin_memory()
     q_dev2 = torch.empty_like(q_local)
-    # The engine keeps one plan object and re-plans it every decode step.
-    p2 = dd.CascadePlan(lcfg, tb.indptr, tb.block_ids, tb.num_tokens)
+    # The engine keeps one plan object and re-plans it every decode step (a
+    # prefill plan is built anew each step).
+    p2 = make_plan()
     p2.device_buffer = plan.device_buffer
 
     def e2e_step():
+        nonlocal p2
         q_dev2.copy_(q_host, non_blocking=True)  # in flight while the host plans
-        p2.rebuild(tb.indptr, tb.block_ids, tb.num_tokens)
+        if pb is not None:
+            buf = p2.device_buffer
+            p2 = make_plan()
+            p2.device_buffer = buf
+        else:
+            p2.rebuild(tb.indptr, tb.block_ids, tb.num_tokens)
         p2.upload(dev)
         r = decode(p2, q_dev2)
         out_host.copy_(r, non_blocking=True)

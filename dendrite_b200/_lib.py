@@ -95,6 +95,8 @@ SIGNATURES = {
     "dd_validate_config": (C.c_int, [_CFGP]),
     "dd_plan_create": (C.c_int, [_CFGP, C.c_int32, _I32P, _U32P, _I32P,
                                  C.POINTER(PlanOptions), C.POINTER(_VP)]),
+    "dd_plan_create_prefill": (C.c_int, [_CFGP, C.c_int32, _I32P, _U32P, _I32P, _I32P,
+                                         C.POINTER(PlanOptions), C.POINTER(_VP)]),
     "dd_plan_destroy": (None, [_VP]),
     "dd_plan_rebuild": (C.c_int, [C.c_void_p, C.c_int32, _I32P, _U32P, _I32P]),
     "dd_plan_get_info": (C.c_int, [_VP, C.POINTER(PlanInfo)]),

@@ -15,8 +15,10 @@ as ``ReferenceBackend`` (backend.rs:161-302):
 KV lives in a device page pool ``[num_pages][2][Hkv][16][D]`` (the layout of
 ``Page``, crates/dendrite-core/src/cache/paged.rs:57). ``decode_batch`` builds
 a cascade plan from the batch's block tables, so every shared prefix is read
-once per batch. ``prefill`` (backend.rs:163-204) is not on the decode path and
-raises ``NotAvailable``.
+once per batch. ``prefill`` (backend.rs:163-204) is the same causal attention
+over pages: it stores the new tokens' K/V in the block table's pages and runs
+a causal plan (``CascadePlan.prefill``) in which new token i sees the
+sequence's tokens up to its own position.
 
 PyTorch is used only for device memory and the current CUDA stream; all
 arithmetic runs in the CUDA kernels of ``libdendrite_b200.so``.
@@ -136,6 +138,32 @@ class CascadePlan:
         check(rc, "dd_plan_create")
         self._h = h
         self.device_buffer = None
+
+    @classmethod
+    def prefill(cls, cfg: AttnConfig, indptr, block_ids, prefix_len, num_new,
+                use_tensor_cores: bool = True) -> "CascadePlan":
+        """Causal prefill plan (dd_plan_create_prefill): sequence s's last
+        num_new[s] tokens are queries seeing tokens [0, prefix_len[s] + i];
+        queries are numbered sequence-major."""
+        self = cls.__new__(cls)
+        self.cfg = cfg
+        self._indptr = np.ascontiguousarray(indptr, dtype=np.int32)
+        self._ids = np.ascontiguousarray(block_ids, dtype=np.uint32)
+        self._prefix = np.ascontiguousarray(prefix_len, dtype=np.int32)
+        self._new = np.ascontiguousarray(num_new, dtype=np.int32)
+        self._ntok = self._prefix + self._new
+        self.batch_size = int(self._new.sum())
+        opts = PlanOptions(1, 0, 1 if use_tensor_cores else 0, 0)
+        h = C.c_void_p()
+        rc = lib.dd_plan_create_prefill(C.byref(cfg), len(self._new),
+                                        self._indptr.ctypes.data_as(_lib._I32P),
+                                        self._ids.ctypes.data_as(_lib._U32P) if len(self._ids) else None,
+                                        self._prefix.ctypes.data_as(_lib._I32P),
+                                        self._new.ctypes.data_as(_lib._I32P), C.byref(opts), C.byref(h))
+        check(rc, "dd_plan_create_prefill")
+        self._h = h
+        self.device_buffer = None
+        return self
 
     @classmethod
     def from_tables(cls, cfg: AttnConfig, tables, **kw) -> "CascadePlan":
@@ -387,8 +415,48 @@ class B200Backend:
         self.kv_dtype = fmt
 
     # -- attention --------------------------------------------------------
-    async def prefill(self, *args, **kw):  # backend.rs:163-204 — not on the decode path
-        raise NotAvailable("prefill is not implemented by the B200 decode backend")
+    def prefill(self, query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,
+                block_table: BlockTable, config: AttentionConfig) -> torch.Tensor:
+        """backend.rs:163-204: causal attention of query [1, Hq, S, D] over
+        key / value [1, Hkv, S, D], over pages. block_table already counts the
+        S new tokens: they are its last S, after prefix_len = num_tokens - S
+        earlier tokens that every new token also sees (0 for the reference's
+        dense prefill). Their K/V are stored into its pages (as append_kv
+        would), then one causal plan runs over the pages."""
+        S = query.shape[2]
+        prefix = block_table.num_tokens() - S
+        if prefix < 0:
+            raise _lib.InvalidArgument("block_table must count the prefill tokens (num_tokens >= seq_len)")
+        if block_table.num_blocks() * PAGE_SIZE < prefix + S:
+            raise _lib.InvalidArgument("block_table has too few blocks for the prefill tokens")
+        if S == 0:
+            return query.clone()
+        pos = torch.arange(prefix, prefix + S)
+        blocks = torch.tensor(block_table.blocks(), dtype=torch.int32)
+        page_ids = blocks[pos // PAGE_SIZE].to(self.device)
+        slots = (pos % PAGE_SIZE).to(torch.int32).to(self.device)
+        k = key.reshape(self.num_kv_heads, S, self.head_dim).transpose(0, 1).contiguous()
+        v = value.reshape(self.num_kv_heads, S, self.head_dim).transpose(0, 1).contiguous()
+        src_dt = torch.float32 if k.dtype == torch.float32 else torch.bfloat16
+        k, v = k.to(src_dt), v.to(src_dt)
+        pool_cfg = make_config(self.num_kv_heads, self.num_kv_heads, self.head_dim, self.num_pages,
+                               DTYPE_F32 if self.pages.dtype == torch.float32 else DTYPE_BF16)
+        append_kv_batch(pool_cfg, self.pages, None, page_ids, slots, k.to(self.pages.dtype),
+                        v.to(self.pages.dtype))
+        if self.codes is not None:  # FP8 pages: quantize the new tokens in place too
+            fp8_cfg = make_config(self.num_kv_heads, self.num_kv_heads, self.head_dim, self.num_pages,
+                                  _KV_DTYPES[self.kv_dtype])
+            append_kv_batch(fp8_cfg, self.codes, self.scales, page_ids, slots, k, v)
+        q = query.reshape(config.num_heads, S, config.head_dim).transpose(0, 1)
+        qd = torch.float32 if q.dtype == torch.float32 else torch.bfloat16
+        q = q.to(qd).contiguous()
+        cfg = self._cfg(config, qd)
+        plan = CascadePlan.prefill(cfg, [0, block_table.num_blocks()], block_table.blocks(), [prefix], [S])
+        plan.upload(self.device)
+        kv, sc = self._kv()
+        ws = _alloc_ws(plan.info().workspace_bytes, self.device, self._ws)
+        out, _ = cascade_decode(cfg, plan, q, kv, sc, workspace=ws)
+        return out.transpose(0, 1).reshape(query.shape).to(query.dtype)
 
     def _kv(self):
         if self.kv_dtype in ("e4m3", "mxfp8"):

@@ -135,6 +135,7 @@ extern "C" int dd_cascade_decode(const dd_attn_config* cfg, const dd_plan* p, co
   AttnArgs a = base_args(cfg, q, kv, scales, ws, (size_t)p->num_slots);
   a.pages = reinterpret_cast<const uint32_t*>(base + p->off_pages);
   a.qorder = reinterpret_cast<const int32_t*>(base + p->off_qorder);
+  a.qlimit = p->causal ? reinterpret_cast<const int32_t*>(base + p->off_qlimit) : nullptr;
   // The tensor-core kernel (wide shared nodes, compute-bound) runs on a side
   // stream forked from `st`, concurrently with the streaming kernel (narrow
   // nodes, HBM-bound); the merge waits for both. The fork/join is a pair of

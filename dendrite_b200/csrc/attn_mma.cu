@@ -203,7 +203,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
         if (pf_idx < a.num_items) {
           pf_it = resolve_item_idx(a, pf_idx, pf_pages, kMmaRows);
           pf_sole = a.items ? (pf_it.nrows & kItemSoleReader) != 0 : a.row_tiles == 1;
-          pf_it.nrows &= kItemRowsMask;
+          pf_it.nrows &= ~kItemSoleReader;  // the causal flag travels to the consumer
         }
       } else if (pf_state == 2) {
         if (pf_idx < a.num_items) {
@@ -211,7 +211,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
           pf_id2 = lane + 32 < pf_it.npages ? pf_pages[lane + 32] : 0u;
         }
       } else if (pf_state == 3) {
-        if (pf_idx < a.num_items && lane < pf_it.nrows) {
+        if (pf_idx < a.num_items && lane < (pf_it.nrows & kItemRowsMask)) {
           const int qi = (pf_it.row0 + lane) / a.g;
           pf_qid = a.qorder ? a.qorder[pf_it.q_begin + qi] : pf_it.q_begin + qi;
         }
@@ -301,7 +301,8 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
             invalid |= 1 << j;
             pg[j] = 0;  // load something harmless; the consumer skips the page
           }
-        const uint32_t qbytes = need_item ? (uint32_t)it.nrows * D * 2 : 0u;
+        const int nrows = it.nrows & kItemRowsMask;
+        const uint32_t qbytes = need_item ? (uint32_t)nrows * D * 2 : 0u;
         const uint32_t bytes = (uint32_t)np * 2 * (C::kSliceRaw + C::kMxBytes) + qbytes;
         if (lane == 0) {
           if (need_item) sh.items[k] = it;
@@ -317,7 +318,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
         __syncwarp();
         // Lane r < nrows copies query row r; lane 16 + 2j + kv copies page
         // j's K (kv = 0) or V slice.
-        if (qbytes && lane < it.nrows) {
+        if (qbytes && lane < nrows) {
           const int rr = it.row0 + lane;
           const int hq = qo_head_of(a.gqa_map, it.kv_head, rr % a.g, a.Hkv, a.g);
           bulk_load(qbuf + lane * C::kQRowBytes,
@@ -378,6 +379,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
     float o[D / 8][4];
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
     float sc_k = 1.f, sc_v = 1.f;  // per-head E4M3 scales of the current item
+    int lim0 = INT_MAX, lim1 = INT_MAX;  // causal plans: tokens seen by rows lane/4, +8
     int items_started = 0;
     long long t_full = 0;
     DD_TSTART(tclife)
@@ -392,6 +394,8 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
       if (m.flags & kDone) break;
       if (m.flags & kFirst) {
         it = sh.items[m.item_slot];
+        const bool causal = (it.nrows & kItemCausal) != 0;
+        it.nrows &= kItemRowsMask;
         if (KV == kKvBf16) {
           const uint32_t qbase = smem_u32(qbuf);
 #pragma unroll
@@ -425,6 +429,12 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
         if (KV == kKvE4m3) {
           sc_k = reinterpret_cast<const float*>(a.scales)[it.kv_head];
           sc_v = reinterpret_cast<const float*>(a.scales)[a.Hkv + it.kv_head];
+        }
+        lim0 = lim1 = INT_MAX;
+        if (causal) {
+          const int r0 = lane >> 2, r1 = r0 + 8;
+          lim0 = r0 < it.nrows ? a.qlimit[it.q_begin + (it.row0 + r0) / a.g] : INT_MAX;
+          lim1 = r1 < it.nrows ? a.qlimit[it.q_begin + (it.row0 + r1) / a.g] : INT_MAX;
         }
       }
       const int np = m.np;
@@ -522,9 +532,12 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
         for (int nt = 0; nt < 4; ++nt) {
           const int vj = valid[nt >> 1];
           const int tok = (nt & 1) * 8 + tc;
+          // Causal plans: token index within the node (items start at its
+          // first token) against each row's limit.
+          const int abs0 = (m.page0 + (nt >> 1)) * kPageSize + tok;
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
-            const bool ok = tok + (c & 1) < vj;
+            const bool ok = tok + (c & 1) < vj && abs0 + (c & 1) < (c < 2 ? lim0 : lim1);
             sacc[nt][c] = ok ? sacc[nt][c] * a.scale_log2 : -INFINITY;
           }
           mx0 = fmaxf(mx0, fmaxf(sacc[nt][0], sacc[nt][1]));

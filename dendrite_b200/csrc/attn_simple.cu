@@ -49,7 +49,9 @@ __global__ void __launch_bounds__(kSimpleThreads) attn_simple_kernel(AttnArgs a)
   float* arow = lrow + kSimpleRows;
 
   const uint32_t* pages;
-  const WorkItem it = resolve_item(a, pages, kSimpleRows);
+  WorkItem it = resolve_item(a, pages, kSimpleRows);
+  const bool causal = a.items && (it.nrows & kItemCausal) != 0;
+  it.nrows &= kItemRowsMask;
   const int tid = threadIdx.x;
   const int nrows = it.nrows;
   if (nrows <= 0) return;
@@ -92,7 +94,8 @@ __global__ void __launch_bounds__(kSimpleThreads) attn_simple_kernel(AttnArgs a)
     for (int idx = tid; idx < nrows * kPageSize; idx += kSimpleThreads) {
       const int r = idx / kPageSize, t = idx % kPageSize;
       float s = -INFINITY;
-      if (t < valid) {
+      const bool seen = !causal || pi * kPageSize + t < a.qlimit[it.q_begin + (it.row0 + r) / a.g];
+      if (t < valid && seen) {
         float acc = 0.f;
         const float* qr = qs + r * D;
         const float* kr = ks + t * D;

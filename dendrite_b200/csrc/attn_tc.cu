@@ -109,7 +109,9 @@ __global__ void __launch_bounds__(TcCfg<KV>::kThreads, 1)
   uint8_t* stages = slots + kTcSlots * kTcSlotBytes;  // FP8: [stage][128 rows][128 B]
   uint8_t* stage_exps = stages + kTcStages * kTcStageCodes;  // [stage][8 pages][64 B]
 
-  const WorkItem it = a.items[blockIdx.x];
+  WorkItem it = a.items[blockIdx.x];
+  const bool causal = (it.nrows & kItemCausal) != 0;
+  it.nrows &= kItemRowsMask;
   const uint32_t* pages = a.pages + it.page_off;
   const int npages = it.npages;
   const int ntiles = (npages + kTcPagesPerTile - 1) / kTcPagesPerTile;
@@ -371,6 +373,9 @@ __global__ void __launch_bounds__(TcCfg<KV>::kThreads, 1)
     }
     const bool active = x == 0 || has_b;
     const float scale_log2 = a.scale_log2;
+    // Causal plans: tokens of the node this row sees (items start at the
+    // node's first token).
+    const int row_lim = causal && live ? a.qlimit[it.q_begin + (it.row0 + row) / a.g] : INT_MAX;
     float m_used = -INFINITY;
     uint64_t lsum = 0ull;  // running row sum, as two packed partial sums
     for (int j = 0; active && j < ntiles; ++j) {
@@ -382,8 +387,9 @@ __global__ void __launch_bounds__(TcCfg<KV>::kThreads, 1)
       mbar_arrive(&bars.p_full[x]);
       continue;
 #endif
-      const int valid = (j == ntiles - 1) ? (npages - kTcPagesPerTile * j - 1) * kPageSize + it.last_valid
-                                          : kTcTok;
+      const int valid = min((j == ntiles - 1) ? (npages - kTcPagesPerTile * j - 1) * kPageSize + it.last_valid
+                                              : kTcTok,
+                            row_lim == INT_MAX ? kTcTok : max(row_lim - kTcTok * j, 0));
       // Pass 1: row max of the raw scores (the scale is positive).
       float mx = -INFINITY;
 #pragma unroll

@@ -4,6 +4,7 @@
 
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <climits>
 #include <cuda_fp8.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -300,6 +301,9 @@ struct AttnArgs {
   const uint32_t* pages;   // plan page list (cascade) / page_indices (flat)
   const int32_t* qorder;   // DFS position -> query (NULL: identity)
   const WorkItem* items;   // cascade items (NULL: flat mode)
+  // Causal (prefill) plans: tokens of its node (from the node's first token,
+  // where every item starts) visible to each DFS query; NULL: all of them.
+  const int32_t* qlimit;
   // flat mode
   const int32_t* page_indptr;
   const int32_t* num_tokens;

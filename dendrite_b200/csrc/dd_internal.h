@@ -42,10 +42,13 @@ struct WorkItem {
   int32_t slot_base;   // partial-state slot of (node, chunk, query 0, head 0)
 };
 static_assert(sizeof(WorkItem) == 32, "WorkItem layout");
-// Streaming (kItemMma) items: nrows bit 16 marks an item that is the only
-// reader of its pages in the launch (its node has one row tile), which then
-// streams them with an L2 evict-first policy.
+// Item flags in the high bits of nrows (kernels mask with kItemRowsMask):
+//  - kItemSoleReader (streaming items): the only reader of its pages in the
+//    launch (its node has one row tile); streams them L2 evict-first;
+//  - kItemCausal (prefill plans): the item's node is a causal suffix; its row
+//    for DFS query p sees the node's first qlimit[p] tokens.
 constexpr int32_t kItemSoleReader = 1 << 16;
+constexpr int32_t kItemCausal = 1 << 17;
 constexpr int32_t kItemRowsMask = 0xffff;
 
 // Device-side view of an uploaded plan (pointers into the caller's buffer).
@@ -67,6 +70,7 @@ struct Node {
   int32_t page_count = 0;
   int32_t last_valid = kPageSize;
   int32_t depth = 0;
+  bool causal = false;  // prefill suffix: query p sees its first qlimit[p] tokens
 };
 
 }  // namespace dd
@@ -92,6 +96,11 @@ struct dd_plan {
   int64_t kv_tokens_by_kind[dd::kNumItemKinds] = {0, 0, 0, 0, 0};
   int64_t tc_row_tokens = 0;
   int32_t max_depth = 0;
+  // Causal (prefill) plans: tokens of its node visible to each DFS query;
+  // items then cover their node from its first token and are not split.
+  bool causal = false;
+  std::vector<int32_t> qlimit;
+  size_t off_qlimit = 0;
   // Packed host image of everything the device needs, and its layout.
   std::vector<uint8_t> image;
   size_t off_items[dd::kNumItemKinds] = {0, 0, 0, 0, 0};

@@ -135,6 +135,8 @@ static void reset_plan(dd_plan* p) {
   p->num_slots = p->kv_tokens = p->kv_tokens_flat = p->tc_row_tokens = 0;
   for (auto& k : p->kv_tokens_by_kind) k = 0;
   p->max_depth = 0;
+  p->causal = false;
+  p->qlimit.clear();
   p->device_base = nullptr;
   p->device_id = -1;
   if (!p->scratch) p->scratch = new PlanScratch();
@@ -356,6 +358,7 @@ static void build_items(dd_plan* p) {
       k = std::max<int64_t>(k, std::min<int64_t>({target, (int64_t)4, std::max<int64_t>(1, n.page_count / 32)}));
     }
     k = std::max<int64_t>(1, std::min<int64_t>(k, n.page_count));
+    if (n.causal) k = 1;  // items start at the node's first token
     sc.node_k[ni] = (int32_t)k;
     sc.node_kind[ni] = kind;
     // Item size of this node for the longest-first order: pages per chunk x
@@ -412,6 +415,13 @@ static void build_items(dd_plan* p) {
           it.kv_head = h;
           it.row0 = (int32_t)(t * rt);
           it.nrows = (int32_t)std::min<int64_t>(rt, rows - t * rt);
+          if (n.causal) {
+            // Only the tokens the tile's last query sees.
+            const int32_t lim = p->qlimit[n.q_begin + (it.row0 + it.nrows - 1) / g];
+            it.npages = (lim + kPageSize - 1) / kPageSize;
+            it.last_valid = lim - (it.npages - 1) * kPageSize;
+            it.nrows |= kItemCausal;
+          }
           if (kind == kItemMma && row_tiles == 1) it.nrows |= kItemSoleReader;
           it.q_begin = n.q_begin;
           it.slot_base = slot_base;
@@ -467,6 +477,7 @@ static void pack_image(dd_plan* p) {
   p->off_pindptr = take(p->path_indptr.size() * sizeof(int32_t));
   p->off_pslots = take(p->path_slots.size() * sizeof(int32_t));
   p->off_groups = take(p->tcs_groups.size() * sizeof(int32_t));
+  p->off_qlimit = take(p->qlimit.size() * sizeof(int32_t));
   // Reused across rebuilds; alignment gaps are never read.
   p->image.resize(std::max<size_t>(off, kAlign));
   auto put = [&](size_t o, const void* src, size_t n) {
@@ -479,6 +490,7 @@ static void pack_image(dd_plan* p) {
   put(p->off_pindptr, p->path_indptr.data(), p->path_indptr.size() * 4);
   put(p->off_pslots, p->path_slots.data(), p->path_slots.size() * 4);
   put(p->off_groups, p->tcs_groups.data(), p->tcs_groups.size() * 4);
+  put(p->off_qlimit, p->qlimit.data(), p->qlimit.size() * 4);
 }
 
 }  // namespace dd
@@ -566,6 +578,119 @@ int dd_plan_rebuild(dd_plan* p, int32_t batch_size, const int32_t* block_indptr,
     p->batch_size = 0;
     return fail(DD_ERR_ALLOCATION, "host allocation failed while planning");
   }
+}
+
+// Causal prefill plan. Sequence s holds prefix_len[s] + num_new[s] tokens;
+// its new tokens are queries (numbered sequence-major) and new token i sees
+// tokens [0, prefix_len[s] + i]. The full pages of the prefixes form a radix
+// tree (shared prefix pages are read once for all the new tokens below them,
+// with no mask); below it, each sequence has a causal node that starts at
+// the page holding token prefix_len[s] (so a partial prefix page is part of
+// it) and whose query i sees its first prefix_len[s] % 16 + i + 1 tokens.
+int dd_plan_create_prefill(const dd_attn_config* cfg, int32_t num_seqs, const int32_t* block_indptr,
+                           const uint32_t* block_ids, const int32_t* prefix_len,
+                           const int32_t* num_new, const dd_plan_options* opts,
+                           dd_plan** out_plan) {
+  if (!out_plan) return fail(DD_ERR_INVALID_ARGUMENT, "out_plan is NULL");
+  *out_plan = nullptr;
+  int st = check_config(cfg);
+  if (st) return st;
+  if (num_seqs < 0) return fail(DD_ERR_INVALID_ARGUMENT, "num_seqs must be >= 0");
+  if (num_seqs > 0 && (!block_indptr || !prefix_len || !num_new))
+    return fail(DD_ERR_INVALID_ARGUMENT, "block_indptr / prefix_len / num_new is NULL");
+  if (num_seqs > 0 && block_indptr[num_seqs] > 0 && !block_ids)
+    return fail(DD_ERR_INVALID_ARGUMENT, "block_ids is NULL");
+  int64_t total = 0;
+  for (int s = 0; s < num_seqs; ++s) {
+    const int64_t nb = (int64_t)block_indptr[s + 1] - block_indptr[s];
+    if (nb < 0) return fail(DD_ERR_INVALID_ARGUMENT, "block_indptr must be non-decreasing");
+    if (prefix_len[s] < 0 || num_new[s] < 0) return fail(DD_ERR_INVALID_ARGUMENT, "prefix_len / num_new must be >= 0");
+    if ((int64_t)prefix_len[s] + num_new[s] > nb * kPageSize)
+      return fail(DD_ERR_INVALID_ARGUMENT, "prefix_len + num_new of sequence " + std::to_string(s) +
+                                               " exceeds its block table");
+    total += num_new[s];
+  }
+  if (total > INT32_MAX) return fail(DD_ERR_INVALID_ARGUMENT, "too many prefill tokens");
+  dd_plan* p = new (std::nothrow) dd_plan();
+  if (!p) return fail(DD_ERR_ALLOCATION, "host allocation failed");
+  p->cfg = *cfg;
+  if (p->cfg.scale <= 0.f) p->cfg.scale = 1.0f / std::sqrt((float)cfg->head_dim);
+  p->opts = opts ? *opts : dd_plan_options{1, 0, 1, 0};
+  p->opts.cta_pairs = 0;  // the CTA-pair kernel has no causal mask
+  try {
+    reset_plan(p);
+    // 1. Radix tree over the sequences' full prefix pages (queries =
+    //    sequences for now).
+    std::vector<int32_t> full((size_t)num_seqs);
+    for (int s = 0; s < num_seqs; ++s) full[s] = (prefix_len[s] / kPageSize) * kPageSize;
+    p->batch_size = num_seqs;
+    st = build_nodes(p, block_indptr, block_ids, full.data());
+    if (st) {
+      delete p;
+      return st;
+    }
+    // 2. Re-number queries: sequence at DFS position d owns new-token
+    //    queries [qd[d], qd[d + 1]).
+    const std::vector<int32_t> seq_order = p->query_order;
+    std::vector<int32_t> qd((size_t)num_seqs + 1, 0), base((size_t)num_seqs + 1, 0);
+    for (int d = 0; d < num_seqs; ++d) qd[d + 1] = qd[d] + num_new[seq_order[d]];
+    for (int s = 0; s < num_seqs; ++s) base[s + 1] = base[s] + num_new[s];
+    std::vector<int32_t> deepest((size_t)num_seqs, -1);
+    for (size_t ni = 0; ni < p->nodes.size(); ++ni) {
+      Node& n = p->nodes[ni];
+      for (int32_t d = n.q_begin; d < n.q_begin + n.num_q; ++d) deepest[d] = (int32_t)ni;
+      const int32_t b0 = qd[n.q_begin], b1 = qd[n.q_begin + n.num_q];
+      n.q_begin = b0;
+      n.num_q = b1 - b0;
+    }
+    p->batch_size = (int32_t)total;
+    p->causal = true;
+    p->query_order.assign((size_t)total, 0);
+    p->qlimit.assign((size_t)total, 0);
+    p->kv_tokens_flat = 0;
+    // 3. One causal node per sequence with new tokens.
+    for (int d = 0; d < num_seqs; ++d) {
+      const int s = seq_order[d];
+      const int32_t n_new = num_new[s], pre = prefix_len[s];
+      for (int32_t i = 0; i < n_new; ++i) {
+        p->query_order[qd[d] + i] = base[s] + i;
+        p->qlimit[qd[d] + i] = pre % kPageSize + i + 1;
+      }
+      p->kv_tokens_flat += (int64_t)n_new * pre + (int64_t)n_new * (n_new + 1) / 2;
+      if (n_new == 0) continue;
+      const int32_t first = pre / kPageSize, end = (pre + n_new + kPageSize - 1) / kPageSize;
+      const uint32_t* ids = block_ids + block_indptr[s];
+      for (int32_t i = first; i < end; ++i)
+        if (ids[i] >= (uint32_t)cfg->num_pages) {
+          delete p;
+          return fail(DD_ERR_INVALID_ARGUMENT, "invalid block id: " + std::to_string(ids[i]));
+        }
+      Node n;
+      n.parent = deepest[d];
+      n.depth = n.parent < 0 ? 0 : p->nodes[n.parent].depth + 1;
+      n.q_begin = qd[d];
+      n.num_q = n_new;
+      n.num_tokens = pre % kPageSize + n_new;
+      n.page_off = (int32_t)p->pages.size();
+      n.page_count = end - first;
+      n.last_valid = pre + n_new - (end - 1) * kPageSize;
+      n.causal = true;
+      p->pages.insert(p->pages.end(), ids + first, ids + end);
+      p->nodes.push_back(n);
+      p->max_depth = std::max(p->max_depth, n.depth + 1);
+    }
+    build_items(p);
+    if (p->num_slots > INT32_MAX) {
+      delete p;
+      return fail(DD_ERR_INVALID_ARGUMENT, "plan too large (partial slots exceed 2^31)");
+    }
+    pack_image(p);
+  } catch (const std::bad_alloc&) {
+    delete p;
+    return fail(DD_ERR_ALLOCATION, "host allocation failed while planning");
+  }
+  *out_plan = p;
+  return DD_OK;
 }
 
 void dd_plan_destroy(dd_plan* plan) { delete plan; }

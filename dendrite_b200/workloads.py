@@ -209,6 +209,60 @@ def llama3_70b_long(seed: int = 0xD3D1, branches: int = 256) -> TreeBatch:
     return build_tree("llama3-70b-131k", 64, 8, 128, 131072, [], branches, (256, 256), seed)
 
 
+@dataclass
+class PrefillBatch:
+    """Chunked prefill of branch suffixes: sequence s holds prefix_len[s] +
+    num_new[s] tokens in its CSR block table; its num_new[s] new tokens are
+    the queries (sequence-major)."""
+
+    name: str
+    num_qo_heads: int
+    num_kv_heads: int
+    head_dim: int
+    num_pages: int
+    indptr: np.ndarray      # int32 [S+1]
+    block_ids: np.ndarray   # uint32
+    prefix_len: np.ndarray  # int32 [S]
+    num_new: np.ndarray     # int32 [S]
+    unique_tokens: int      # KV tokens, shared prefix pages counted once
+
+    def nested(self) -> TreeBatch:
+        """The same work as a decode batch: new token i of sequence s is a
+        query over the sequence's table with prefix_len[s] + i + 1 tokens."""
+        ptr, ids, ntok = [0], [], []
+        for s in range(len(self.num_new)):
+            tbl = self.block_ids[self.indptr[s]:self.indptr[s + 1]]
+            for i in range(int(self.num_new[s])):
+                ids.append(tbl)
+                ptr.append(ptr[-1] + len(tbl))
+                ntok.append(int(self.prefix_len[s]) + i + 1)
+        return TreeBatch(self.name + "-nested", self.num_qo_heads, self.num_kv_heads, self.head_dim,
+                         self.num_pages, np.array(ptr, np.int32),
+                         np.concatenate(ids).astype(np.uint32) if ids else np.zeros(0, np.uint32),
+                         np.array(ntok, np.int32), self.unique_tokens)
+
+
+def prefill_branches_8b(seed: int = 0xD3D1, prefix: int = 8192, branches: int = 16,
+                        new: int = 64) -> PrefillBatch:
+    """Llama-3-8B heads (Hq32/Hkv8/D128): one shared prefix, then `branches`
+    forks that each prefill `new` tokens (TreeState fork + append semantics:
+    a partial last prefix page is copied on write)."""
+    rng = np.random.default_rng(seed)
+    pages = -(-prefix // PAGE) + branches * (-(-new // PAGE) + 1)
+    pool = BlockPool(pages, rng)
+    tb = TreeBuilder(pool)
+    root = tb.root(prefix)
+    seqs = []
+    for _ in range(branches):
+        c = tb.fork(root)
+        tb.append(c, new)
+        seqs.append(c)
+    indptr, ids, _ = _csr(seqs)
+    return PrefillBatch(f"prefill-llama3-8b-{prefix}+{branches}x{new}", 32, 8, 128, pages, indptr, ids,
+                        np.full(branches, prefix, np.int32), np.full(branches, new, np.int32),
+                        prefix + branches * new)
+
+
 def small_tree(seed: int, Hq: int = 8, Hkv: int = 2, D: int = 128, prefix: int = 64,
                levels=((2, 16, 48),), leaves_per_node: int = 3, suffix=(1, 40)) -> TreeBatch:
     """Small random trees for parity tests."""

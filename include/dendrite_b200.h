@@ -154,6 +154,23 @@ int dd_plan_create(const dd_attn_config* cfg, int32_t batch_size,
                    const int32_t* num_tokens, const dd_plan_options* opts,
                    dd_plan** out_plan);
 void dd_plan_destroy(dd_plan* plan);
+/* Causal prefill plan over paged KV (chunked prefill of branch suffixes):
+ * sequence s holds prefix_len[s] + num_new[s] tokens in its block table
+ * block_ids[block_indptr[s] .. block_indptr[s+1]), the last num_new[s] of
+ * them new (their K/V already stored, e.g. by dd_append_kv_batch). Its new
+ * token i is a query that sees tokens [0, prefix_len[s] + i] of the sequence;
+ * queries are numbered sequence-major, so q / out of dd_cascade_decode are
+ * [sum(num_new)][num_qo_heads][head_dim]. With prefix_len = 0 this is
+ * ReferenceBackend::prefill's causal attention
+ * (crates/dendrite-core/src/attention/backend.rs:163-204) over pages; the
+ * stub it replaces is BatchPrefillKernel::run
+ * (crates/dendrite-ffi/src/flashinfer/batch_prefill.rs). Each sequence's
+ * pages are read once per row tile of its queries; dd_plan_rebuild turns the
+ * plan back into a decode plan. */
+int dd_plan_create_prefill(const dd_attn_config* cfg, int32_t num_seqs,
+                           const int32_t* block_indptr, const uint32_t* block_ids,
+                           const int32_t* prefix_len, const int32_t* num_new,
+                           const dd_plan_options* opts, dd_plan** out_plan);
 /* Re-plans an existing plan for a new decode batch (same config and
  * options), reusing its host memory: the per-step call of an engine whose
  * tree grows by one token per leaf per step. The device image must be

@@ -35,12 +35,13 @@ def _cpu_has_v3() -> bool:
 def _load():
     name = "liboracle_v3.so" if _cpu_has_v3() else "liboracle_generic.so"
     path = HERE / name
-    if not path.exists():
+    if not path.exists() or path.stat().st_mtime < (HERE / "dd_oracle.c").stat().st_mtime:
         from . import build as _b  # build recipe lives beside the source
         _b.build()
     lib = C.CDLL(str(path))
     vp, i64 = C.c_void_p, C.c_int64
     sig = {
+        "or_prefill": (None, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_float, vp, vp, vp, vp]),
         "or_decode_batch": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_float, vp,
                                       C.c_int, i64, vp, vp, vp, vp, vp, vp, C.c_int]),
         "or_merge_states": (None, [C.c_int, C.c_int, vp, vp, vp, vp, vp, vp]),
@@ -130,6 +131,18 @@ def dequantize(codes: np.ndarray, scales: np.ndarray, fmt: str, out: str = "bf16
     lib.or_dequant(_p(codes), 3 if fmt == "e4m3" else 4, _p(sc), P, Hkv, D, _p(o),
                    1 if out == "bf16" else 2)
     return o
+
+
+def prefill(q: np.ndarray, k: np.ndarray, v: np.ndarray, scale: float = 0.0) -> np.ndarray:
+    """ReferenceBackend::prefill (backend.rs:163-204), batch 1: q [Hq][S][D],
+    k, v [Hkv][S][D] f32 -> causal attention output [Hq][S][D] f32."""
+    q = np.ascontiguousarray(q, dtype=np.float32)
+    k = np.ascontiguousarray(k, dtype=np.float32)
+    v = np.ascontiguousarray(v, dtype=np.float32)
+    Hq, S, D = q.shape
+    out = np.empty((Hq, S, D), dtype=np.float32)
+    lib.or_prefill(S, Hq, k.shape[0], D, scale, _p(q), _p(k), _p(v), _p(out))
+    return out
 
 
 def decode_batch(q: np.ndarray, pool: np.ndarray, indptr, block_ids, num_tokens, num_kv_heads: int,

@@ -317,6 +317,45 @@ int or_decode_batch(int B, int Hq, int Hkv, int D, int gqa_grouped, float scale,
   return 0;
 }
 
+/* ReferenceBackend::prefill (crates/dendrite-core/src/attention/backend.rs:
+ * 163-204) for batch 1: q [Hq][S][D], k, v [Hkv][S][D] f32. GQA by
+ * Tensor::repeat (tiled: head h reads KV head h % Hkv, :176-183); scores
+ * q.k^T * scale (:185-187) plus the causal mask, 0 on and below the diagonal
+ * and -inf above (create_causal_mask, :146-158); softmax over the keys
+ * (max-subtract, exp, sum, divide); @ v. out [Hq][S][D]. */
+void or_prefill(int S, int Hq, int Hkv, int D, float scale, const float* q, const float* k,
+                const float* v, float* out) {
+  const float sc_f = scale > 0.0f ? scale : 1.0f / sqrtf((float)D);
+  float* sc = (float*)malloc(sizeof(float) * (S ? S : 1));
+  if (!sc) return;
+  for (int h = 0; h < Hq; ++h) {
+    const int src = h % Hkv;
+    const float* kh = k + (size_t)src * S * D;
+    const float* vh = v + (size_t)src * S * D;
+    for (int i = 0; i < S; ++i) {
+      const float* qi = q + ((size_t)h * S + i) * D;
+      float mx = -INFINITY;
+      for (int jj = 0; jj < S; ++jj) {
+        float acc = 0.0f;
+        for (int d = 0; d < D; ++d) acc += qi[d] * kh[(size_t)jj * D + d];
+        sc[jj] = acc * sc_f + (jj > i ? -INFINITY : 0.0f);
+        if (sc[jj] > mx) mx = sc[jj];
+      }
+      float sum = 0.0f;
+      for (int jj = 0; jj < S; ++jj) {
+        sc[jj] = expf(sc[jj] - mx);
+        sum += sc[jj];
+      }
+      for (int jj = 0; jj < S; ++jj) sc[jj] /= sum;
+      float* o = out + ((size_t)h * S + i) * D;
+      for (int d = 0; d < D; ++d) o[d] = 0.0f;
+      for (int jj = 0; jj < S; ++jj)
+        for (int d = 0; d < D; ++d) o[d] += sc[jj] * vh[(size_t)jj * D + d];
+    }
+  }
+  free(sc);
+}
+
 /* merge_attention_outputs (cascade.rs:116-124), element-wise over n rows of D. */
 void or_merge_states(int n, int D, const float* o1, const float* l1, const float* o2,
                      const float* l2, float* o, float* l) {
