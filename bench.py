@@ -70,6 +70,7 @@ WORKLOADS = {
                         desc="config 2: MXFP8 quantize of 4096 x [2][4][16][64] bf16 pages"),
 }
 QUANT_PAGES, QUANT_HKV, QUANT_D = 4096, 4, 64
+E2E_MAX_STEPS = 3 + 30  # warm-up + timed steps of the end-to-end loop (e2e_time)
 
 
 def peaks():
@@ -407,7 +408,10 @@ def run_tree(args, world, rank, local, dev):
     Hq, Hkv, D, B = tb.num_qo_heads, tb.num_kv_heads, tb.head_dim, tb.batch_size
     gen = torch.Generator(device=dev)
     gen.manual_seed(SEED if heads else SEED + rank)
-    pool = torch.randn((tb.num_pages, 2, Hkv, 16, D), generator=gen, device=dev,
+    # Spare pages for the end-to-end loop, whose leaves grow a token a step.
+    spare = B * (E2E_MAX_STEPS // 16 + 2)
+    num_pages = tb.num_pages + spare
+    pool = torch.randn((num_pages, 2, Hkv, 16, D), generator=gen, device=dev,
                        dtype=torch.float32).to(torch.bfloat16)
     q = torch.randn((B, Hq, D), generator=gen, device=dev, dtype=torch.float32).to(torch.bfloat16)
     scales = None
@@ -420,7 +424,7 @@ def run_tree(args, world, rank, local, dev):
         scale_bytes = D / 32 if kv == "mxfp8" else 0.0
     else:
         kv_pages = pool
-    cfg = dd.make_config(Hq, Hkv, D, tb.num_pages, kv_dtype=kv_dtype)
+    cfg = dd.make_config(Hq, Hkv, D, num_pages, kv_dtype=kv_dtype)
     if heads:
         lcfg = hs.shard_config(cfg, world)
         kv_local = hs.shard_pages(kv_pages, rank, world)
@@ -501,10 +505,23 @@ def run_tree(args, world, rank, local, dev):
     res = out if heads else out_local
     out_host = torch.empty(res.shape, dtype=res.dtype).pin_memory()
     q_dev2 = torch.empty_like(q_local)
-    # The engine keeps one plan object and re-plans it every decode step (a
-    # prefill plan is built anew each step).
+    # The engine keeps one plan object across decode steps: every leaf grows
+    # by one token a step (a new block from the spare pages when its last one
+    # is full) and the plan is advanced in place (dd_plan_advance), re-planned
+    # from the grown tables only when that is refused. A prefill plan is
+    # built anew each step.
     p2 = make_plan()
     p2.device_buffer = plan.device_buffer
+    ntok_e = tb.num_tokens.astype(np.int64).copy()
+    appended = [[] for _ in range(B)]
+    next_spare = [tb.num_pages]
+    ones = np.ones(B, np.int32)
+
+    def grown_tables():
+        lens = np.diff(tb.indptr) + np.array([len(a) for a in appended])
+        ids = [np.concatenate([tb.block_ids[tb.indptr[b]:tb.indptr[b + 1]],
+                               np.array(appended[b], np.uint32)]) for b in range(B)]
+        return np.concatenate([[0], np.cumsum(lens)]).astype(np.int32), np.concatenate(ids), ntok_e
 
     def e2e_step():
         nonlocal p2
@@ -514,7 +531,15 @@ def run_tree(args, world, rank, local, dev):
             p2 = make_plan()
             p2.device_buffer = buf
         else:
-            p2.rebuild(tb.indptr, tb.block_ids, tb.num_tokens)
+            full = np.nonzero(ntok_e % 16 == 0)[0]
+            new_block = np.zeros(B, np.uint32)
+            new_block[full] = np.arange(next_spare[0], next_spare[0] + len(full))
+            next_spare[0] += len(full)
+            for b in full:
+                appended[b].append(int(new_block[b]))
+            ntok_e[:] += 1
+            if not p2.advance(ones, new_block):
+                p2.rebuild(*grown_tables())
         p2.upload(dev)
         r = decode(p2, q_dev2)
         out_host.copy_(r, non_blocking=True)

@@ -187,6 +187,20 @@ class CascadePlan:
         check(rc, "dd_plan_rebuild")
         return self
 
+    def advance(self, tokens_added, new_block=None) -> bool:
+        """One decode step in place (dd_plan_advance): query b gained
+        tokens_added[b] (0 or 1) tokens, a token that starts a new block went
+        to new_block[b]. False: some query shares its last pages (or the plan
+        is a prefill / flat plan); re-plan with rebuild()."""
+        t = np.ascontiguousarray(tokens_added, dtype=np.int32)
+        nb = None if new_block is None else np.ascontiguousarray(new_block, dtype=np.uint32)
+        rc = lib.dd_plan_advance(self._h, t.ctypes.data_as(_lib._I32P),
+                                 nb.ctypes.data_as(_lib._U32P) if nb is not None else None)
+        if rc == _lib.DD_ERR_NOT_AVAILABLE:
+            return False
+        check(rc, "dd_plan_advance")
+        return True
+
     def __del__(self):
         h = getattr(self, "_h", None)
         if h:

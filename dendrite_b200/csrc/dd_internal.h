@@ -71,6 +71,9 @@ struct Node {
   int32_t last_valid = kPageSize;
   int32_t depth = 0;
   bool causal = false;  // prefill suffix: query p sees its first qlimit[p] tokens
+  // Set by the item builder: kernel kind, split-K chunks, and the node's
+  // items [item_begin, item_begin + item_count) of items[kind].
+  int32_t kind = 0, k = 1, item_begin = 0, item_count = 0;
 };
 
 }  // namespace dd
@@ -101,6 +104,9 @@ struct dd_plan {
   bool causal = false;
   std::vector<int32_t> qlimit;
   size_t off_qlimit = 0;
+  // Deepest node of each DFS query (-1: empty table), for dd_plan_advance.
+  std::vector<int32_t> q_leaf;
+  int64_t live_pages = 0;  // pages referenced by nodes (the rest of `pages` is dead)
   // Packed host image of everything the device needs, and its layout.
   std::vector<uint8_t> image;
   size_t off_items[dd::kNumItemKinds] = {0, 0, 0, 0, 0};

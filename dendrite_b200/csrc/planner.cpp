@@ -396,12 +396,16 @@ static void build_items(dd_plan* p) {
   std::sort(sc.keys.begin(), sc.keys.end());
   for (const auto& key : sc.keys) {
     const size_t ni = (size_t)key.second;
-    const Node& n = p->nodes[ni];
+    Node& n = p->nodes[ni];
     const int64_t rows = (int64_t)n.num_q * g;
     const int kind = sc.node_kind[ni];
     const int rt = row_tile_for(kind);
     const int64_t row_tiles = (rows + rt - 1) / rt;
     const int32_t k = sc.node_k[ni];
+    n.kind = kind;
+    n.k = k;
+    n.item_begin = (int32_t)p->items[kind].size();
+    n.item_count = (int32_t)(k * Hkv * row_tiles);
     for (int32_t ci = 0; ci < k; ++ci) {
       const int32_t pb = (int32_t)((int64_t)ci * n.page_count / k);
       const int32_t pe = (int32_t)((int64_t)(ci + 1) * n.page_count / k);
@@ -428,6 +432,15 @@ static void build_items(dd_plan* p) {
           p->items[kind].push_back(it);
         }
     }
+  }
+  // Deepest node of every DFS query (nodes are in pre-order, so a node's
+  // descendants come after it); pages in use.
+  p->q_leaf.assign((size_t)B, -1);
+  p->live_pages = 0;
+  for (size_t ni = 0; ni < N; ++ni) {
+    const Node& n = p->nodes[ni];
+    p->live_pages += n.page_count;
+    for (int32_t q = n.q_begin; q < n.q_begin + n.num_q; ++q) p->q_leaf[q] = (int32_t)ni;
   }
   // Groups of streaming items: per KV head, consecutive items (longest
   // first) while the group stays within kTcsMaxRows rows and kTcsMaxPages
@@ -693,6 +706,82 @@ int dd_plan_create_prefill(const dd_attn_config* cfg, int32_t num_seqs, const in
   return DD_OK;
 }
 
+// One decode step in place: query b (in the batch's order) gained
+// tokens_added[b] (0 or 1) tokens; a token that starts a new block went to
+// block new_block[b]. Only a query whose deepest node is its own (no other
+// query shares its last pages) can grow in place: its node gains the token
+// (and the block), and the node's items are re-cut. Any other change returns
+// DD_ERR_NOT_AVAILABLE with the plan unchanged; the caller re-plans with
+// dd_plan_rebuild from the full tables.
+int dd_plan_advance(dd_plan* p, const int32_t* tokens_added, const uint32_t* new_block) {
+  if (!p || !tokens_added) return fail(DD_ERR_INVALID_ARGUMENT, "plan / tokens_added is NULL");
+  if (p->causal) return fail(DD_ERR_NOT_AVAILABLE, "prefill plans are not advanced; re-plan");
+  if (!p->opts.share_prefixes) return fail(DD_ERR_NOT_AVAILABLE, "flat plans are not advanced; re-plan");
+  const int B = p->batch_size;
+  PlanScratch& sc = *p->scratch;
+  std::vector<int32_t>& pos = sc.qcursor;  // DFS position of each query
+  pos.assign((size_t)B, 0);
+  for (int d = 0; d < B; ++d) pos[p->query_order[d]] = d;
+  int64_t grow_pages = 0;
+  for (int b = 0; b < B; ++b) {
+    const int32_t t = tokens_added[b];
+    if (t == 0) continue;
+    if (t != 1) return fail(DD_ERR_INVALID_ARGUMENT, "tokens_added must be 0 or 1");
+    const int32_t leaf = p->q_leaf[pos[b]];
+    if (leaf < 0 || p->nodes[leaf].num_q != 1)
+      return fail(DD_ERR_NOT_AVAILABLE, "query " + std::to_string(b) + " shares its last pages; re-plan");
+    if (p->nodes[leaf].last_valid == kPageSize) {
+      if (!new_block) return fail(DD_ERR_INVALID_ARGUMENT, "new_block is NULL");
+      if (new_block[b] >= (uint32_t)p->cfg.num_pages)
+        return fail(DD_ERR_INVALID_ARGUMENT, "invalid block id: " + std::to_string(new_block[b]));
+      grow_pages += p->nodes[leaf].page_count + 1;
+    }
+  }
+  // Moved runs leave dead entries behind; past as many dead as live ids,
+  // re-plan (which compacts).
+  if ((int64_t)p->pages.size() + grow_pages > 2 * (p->live_pages + grow_pages) + 1024)
+    return fail(DD_ERR_NOT_AVAILABLE, "page list needs compaction; re-plan");
+  const int Hkv = p->cfg.num_kv_heads, g = p->cfg.num_qo_heads / Hkv;
+  for (int b = 0; b < B; ++b) {
+    if (tokens_added[b] == 0) continue;
+    Node& n = p->nodes[p->q_leaf[pos[b]]];
+    if (n.last_valid == kPageSize) {
+      // The node's run moves to the end of the page list, followed by the new block.
+      if ((size_t)(n.page_off + n.page_count) != p->pages.size()) {
+        const size_t off = p->pages.size();
+        p->pages.resize(off + n.page_count);
+        std::memcpy(p->pages.data() + off, p->pages.data() + n.page_off, (size_t)n.page_count * 4);
+        n.page_off = (int32_t)off;
+      }
+      p->pages.push_back(new_block[b]);
+      ++n.page_count;
+      ++p->live_pages;
+      n.last_valid = 1;
+    } else {
+      ++n.last_valid;
+    }
+    ++n.num_tokens;
+    ++p->kv_tokens;
+    ++p->kv_tokens_flat;
+    p->kv_tokens_by_kind[n.kind] += 1;
+    // Re-cut the node's items: [chunk][KV head][row tile], as the builder emits them.
+    const int rt = row_tile_for(n.kind);
+    const int32_t row_tiles = (int32_t)((n.num_q * g + rt - 1) / rt);
+    WorkItem* it = p->items[n.kind].data() + n.item_begin;
+    for (int32_t ci = 0; ci < n.k; ++ci) {
+      const int32_t pb = (int32_t)((int64_t)ci * n.page_count / n.k);
+      const int32_t pe = (int32_t)((int64_t)(ci + 1) * n.page_count / n.k);
+      for (int32_t j = 0; j < Hkv * row_tiles; ++j, ++it) {
+        it->page_off = n.page_off + pb;
+        it->npages = pe - pb;
+        it->last_valid = pe == n.page_count ? n.last_valid : kPageSize;
+      }
+    }
+  }
+  pack_image(p);
+  return DD_OK;
+}
+
 void dd_plan_destroy(dd_plan* plan) { delete plan; }
 
 int dd_plan_get_info(const dd_plan* p, dd_plan_info* info) {
@@ -716,16 +805,21 @@ int dd_plan_export_nodes(const dd_plan* p, int32_t* parent, int32_t* q_begin, in
                          int32_t* num_tokens, int32_t* page_offset, int32_t* page_count,
                          uint32_t* pages, int32_t* query_order) {
   if (!p) return fail(DD_ERR_INVALID_ARGUMENT, "plan is NULL");
+  // Pages are exported node after node (offsets into that list), without
+  // the dead runs dd_plan_advance leaves in the plan's own list.
+  int32_t off = 0;
   for (size_t i = 0; i < p->nodes.size(); ++i) {
     const Node& n = p->nodes[i];
     if (parent) parent[i] = n.parent;
     if (q_begin) q_begin[i] = n.q_begin;
     if (num_q) num_q[i] = n.num_q;
     if (num_tokens) num_tokens[i] = n.num_tokens;
-    if (page_offset) page_offset[i] = n.page_off;
+    if (page_offset) page_offset[i] = off;
     if (page_count) page_count[i] = n.page_count;
+    if (pages && n.page_count)
+      std::memcpy(pages + off, p->pages.data() + n.page_off, (size_t)n.page_count * 4);
+    off += n.page_count;
   }
-  if (pages && !p->pages.empty()) std::memcpy(pages, p->pages.data(), p->pages.size() * 4);
   if (query_order && !p->query_order.empty())
     std::memcpy(query_order, p->query_order.data(), p->query_order.size() * 4);
   return DD_OK;

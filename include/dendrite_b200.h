@@ -178,13 +178,27 @@ int dd_plan_create_prefill(const dd_attn_config* cfg, int32_t num_seqs,
  * error the plan is left empty (batch 0). No reference counterpart. */
 int dd_plan_rebuild(dd_plan* plan, int32_t batch_size, const int32_t* block_indptr,
                     const uint32_t* block_ids, const int32_t* num_tokens);
+/* Advances a decode plan by one decode step in place, the per-step call of
+ * an engine whose leaves each grow by a token (the scheduler's plan cache):
+ * query b (batch order) gained tokens_added[b] tokens (0 or 1); a token that
+ * starts a new block went to block new_block[b] (read only for those). In
+ * place only for queries that own their last pages (a leaf of the plan's
+ * tree with no other query): their nodes gain the token / block and their
+ * items are re-cut; the device image must be uploaded again. Returns
+ * DD_ERR_NOT_AVAILABLE, with the plan unchanged, when some query shares its
+ * last pages (a fresh fork, a copy-on-write pending), for prefill and flat
+ * plans, or when the page list needs compacting: the caller then re-plans
+ * with dd_plan_rebuild from the full block tables. No reference counterpart
+ * (the reference re-reads every block table per query and step). */
+int dd_plan_advance(dd_plan* plan, const int32_t* tokens_added, const uint32_t* new_block);
 int dd_plan_get_info(const dd_plan* plan, dd_plan_info* info);
 /* Copies the plan's arrays into caller-owned device memory (>= device_bytes,
  * 256-byte aligned). Must be called before dd_cascade_decode. */
 int dd_plan_upload(dd_plan* plan, void* device_buf, size_t bytes, dd_stream_t stream);
 /* Host view of the plan's nodes, for tests and tooling. Each array may be
- * NULL; non-NULL arrays have num_nodes entries (node_pages: kv_tokens/16+num_nodes
- * upper bound — pass NULL and read node_page_count to size it). */
+ * NULL; non-NULL arrays have num_nodes entries, except node_pages: every
+ * node's pages one node after another (sum of node_page_count entries; pass
+ * NULL and read node_page_count to size it), node_page_offset indexing it. */
 int dd_plan_export_nodes(const dd_plan* plan, int32_t* node_parent,
                          int32_t* node_q_begin, int32_t* node_num_q,
                          int32_t* node_num_tokens, int32_t* node_page_offset,
