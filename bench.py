@@ -111,24 +111,30 @@ def make_tree(name: str, rank: int, world: int):
 
 
 class Clocks:
-    """nvidia-smi sampler (200 ms period) around the timed region. A reader
-    thread collects the samples; `ready()` returns once the first one is in,
-    so the timed steps start with the sampler running, and `stop()` waits for
-    one sample taken after them (a step loop can be shorter than the period)."""
+    """nvidia-smi sampler (200 ms period) around the timed region, one process
+    for all of the job's GPUs (named by UUID, so CUDA_VISIBLE_DEVICES
+    remapping cannot point it at another GPU; rank 0 only, so N samplers do
+    not stall the ranks of a collective in turn). A reader thread collects
+    the samples; `ready()` returns once the first one is in, so the timed
+    steps start with the sampler running, and `stop()` waits for one sample
+    taken after them (a step loop can be shorter than the period)."""
 
-    def __init__(self, device_index: int, out: Path | None):
+    def __init__(self, gpu_ids: str | None, out: Path | None):
         import threading
 
         self.proc = None
         self.path = out
         self.lines: list[str] = []
         self.t_mark = 0
+        self.n_gpus = len(gpu_ids.split(",")) if gpu_ids else 1
+        if gpu_ids is None:
+            return
         q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={device_index}", f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                ["nvidia-smi", f"--id={gpu_ids}", f"--query-gpu={q}", "--format=csv,noheader,nounits",
                  "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except (OSError, FileNotFoundError):
             self.proc = None
@@ -147,15 +153,15 @@ class Clocks:
             time.sleep(0.01)
 
     def ready(self, timeout: float = 5.0):
-        """Block until the sampler has produced its first sample."""
+        """Block until the sampler has produced its first sample (one row per GPU)."""
         if self.proc:
-            self._wait_rows(1, timeout)
+            self._wait_rows(self.n_gpus, timeout)
             self.t_mark = len(self.lines)
 
     def stop(self):
         if not self.proc:
             return None
-        self._wait_rows(self.t_mark + 1, 2.0)  # a sample taken after the timed steps
+        self._wait_rows(self.t_mark + self.n_gpus, 2.0)  # a sample taken after the timed steps
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
@@ -331,9 +337,17 @@ def timed_steps(step, flush, args, world, rank, local, dev):
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    clocks = Clocks(local, ROOT / "gpurun_out" / f"clocks_rank{rank}.csv"
-                    if (ROOT / "gpurun_out").is_dir() else None)
+    uuid = f"GPU-{torch.cuda.get_device_properties(dev).uuid}"
+    uuids = [uuid]
+    if world > 1:
+        uuids = [None] * world
+        dist.all_gather_object(uuids, uuid)
+    clocks = Clocks(",".join(uuids) if rank == 0 else None,
+                    ROOT / "gpurun_out" / "clocks.csv" if (ROOT / "gpurun_out").is_dir() else None)
     clocks.ready()
+    if world > 1:
+        dist.barrier()  # rank 0 waited for the sampler: start the timed steps together
+    torch.cuda.synchronize()
     stream = torch.cuda.current_stream()
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
           for _ in range(args.steps)]

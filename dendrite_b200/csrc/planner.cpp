@@ -351,11 +351,15 @@ static void build_items(dd_plan* p) {
     if ((kind == kItemTc || kind == kItemTc2) && p->opts.max_chunk_pages <= 0) {
       // Wide nodes are compute-bound: split their pages so the tensor-core
       // grid covers the SMs (at least 32 pages per chunk), even though each
-      // chunk adds a partial state per row. A CTA-pair item takes two SMs.
+      // chunk adds a partial state per row (at most 4 chunks, unless fewer
+      // than 37 row tiles x KV heads would leave most SMs idle, as for one
+      // KV head of a long tree per GPU). A CTA-pair item takes two SMs.
       const int64_t per = row_tiles * Hkv;
       const int64_t units = kind == kItemTc2 ? kPlanSms / 2 : kPlanSms;
       const int64_t target = std::max<int64_t>(1, (units + per / 2) / per);
-      k = std::max<int64_t>(k, std::min<int64_t>({target, (int64_t)4, std::max<int64_t>(1, n.page_count / 32)}));
+      // Without the 4-chunk cap, stay within one wave of CTAs.
+      const int64_t cap = per * 4 >= kPlanSms ? 4 : std::max<int64_t>(4, units / per);
+      k = std::max<int64_t>(k, std::min<int64_t>({target, cap, std::max<int64_t>(1, n.page_count / 32)}));
     }
     k = std::max<int64_t>(1, std::min<int64_t>(k, n.page_count));
     if (n.causal) k = 1;  // items start at the node's first token
