@@ -54,7 +54,12 @@ __device__ __forceinline__ float2 e4m3x2_to_float2(uint16_t c2) {
 __device__ __forceinline__ uint8_t float_to_e4m3_satrn(float x) {
   return (uint8_t)__nv_cvt_float_to_fp8(x, __NV_SATFINITE, __NV_E4M3);
 }
-
+// Four of them packed little-endian (a in byte 0), two per conversion.
+__device__ __forceinline__ uint32_t e4m3x4_satrn(float a, float b, float c, float d) {
+  const uint32_t lo = __nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3);
+  const uint32_t hi = __nv_cvt_float2_to_fp8x2(make_float2(c, d), __NV_SATFINITE, __NV_E4M3);
+  return (lo & 0xffffu) | (hi << 16);
+}
 // E8M0 shared exponent byte -> 2^(c-127) as f32 (c = 0 gives 2^-127, a
 // subnormal f32; c = 255 is NaN in the format and is never produced).
 // Branch-free: y = c << 23; c = 0 gives max(0, 2^-127 bits), c = 255 gives

@@ -33,9 +33,11 @@ __device__ __forceinline__ void load8(const void* src, int src_dtype, size_t i, 
 }
 
 // Pass 1 of per-head E4M3: amax per (K/V, KV head) over the whole pool.
-// One warp per page slice ([16][D] elements of one (page, K/V, head)).
+// One warp per page slice ([16][D] elements of one (page, K/V, head)); a
+// lane's D/16 16-byte loads of a slice are issued together.
+template <int D>
 __global__ void amax_per_head_kernel(const void* src, int src_dtype, int64_t nslices, int Hkv,
-                                     int D, uint32_t* amax_bits) {
+                                     uint32_t* amax_bits) {
   __shared__ uint32_t sm[64];
   const int n2 = 2 * Hkv;
   for (int i = threadIdx.x; i < n2; i += blockDim.x) sm[i] = 0;
@@ -43,23 +45,28 @@ __global__ void amax_per_head_kernel(const void* src, int src_dtype, int64_t nsl
   const int lane = threadIdx.x & 31;
   const int64_t warp0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-  const int per = kPageSize * D;
+  constexpr int per = kPageSize * D, kLoads = per / (32 * 8);
   for (int64_t s = warp0; s < nslices; s += nwarps) {
-    float m = 0.f;
-    for (int e = lane * 8; e < per; e += 32 * 8) {
-      float v[8];
-      load8(src, src_dtype, (size_t)s * per + e, v);
+    float v[kLoads][8];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) m = fmaxf(m, fabsf(v[k]));
-    }
+    for (int u = 0; u < kLoads; ++u) load8(src, src_dtype, (size_t)s * per + (u * 32 + lane) * 8, v[u]);
+    float m = 0.f;
+#pragma unroll
+    for (int u = 0; u < kLoads; ++u)
+#pragma unroll
+      for (int k = 0; k < 8; ++k) m = fmaxf(m, fabsf(v[u][k]));
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    if (lane == 0) atomicMax(&sm[s % n2], __float_as_uint(m));
+    if (lane == 0) atomicMax(&sm[(uint32_t)s % (uint32_t)n2], __float_as_uint(m));
   }
   __syncthreads();
   for (int i = threadIdx.x; i < n2; i += blockDim.x)
     if (sm[i]) atomicMax(&amax_bits[i], sm[i]);
 }
+
+// Vectors (8 elements) per thread per round of the quantize kernels: their
+// loads are issued before any is converted.
+constexpr int kQuantUnroll = 4;
 
 __device__ __forceinline__ float head_scale_from_amax(float amax, int mode) {
   if (!(amax > 0.f)) return 1.f;
@@ -77,20 +84,29 @@ __global__ void quant_e4m3_kernel(const void* src, int src_dtype, int64_t nelem,
   __syncthreads();
   if (blockIdx.x == 0)
     for (int i = threadIdx.x; i < n2; i += blockDim.x) scales[i] = ssc[i];
-  const int per = kPageSize * D;
+  const int vec_shift = 31 - __clz(kPageSize * D / 8);  // vectors per page slice = 2 D
   const int64_t nvec = nelem / 8;
-  for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nvec;
-       v += (int64_t)gridDim.x * blockDim.x) {
-    const size_t i = (size_t)v * 8;
-    float x[8];
-    load8(src, src_dtype, i, x);
-    const float sc = ssc[(i / per) % n2];
-    uint32_t lo = 0, hi = 0;
+  const int64_t step = (int64_t)gridDim.x * blockDim.x * kQuantUnroll;
+  for (int64_t base = (int64_t)blockIdx.x * blockDim.x * kQuantUnroll; base < nvec; base += step) {
+    float x[kQuantUnroll][8];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) lo |= (uint32_t)float_to_e4m3_satrn(__fdiv_rn(x[k], sc)) << (8 * k);
+    for (int u = 0; u < kQuantUnroll; ++u) {
+      const int64_t v = base + u * blockDim.x + threadIdx.x;
+      load8(src, src_dtype, (size_t)(v < nvec ? v : 0) * 8, x[u]);
+    }
 #pragma unroll
-    for (int k = 0; k < 4; ++k) hi |= (uint32_t)float_to_e4m3_satrn(__fdiv_rn(x[4 + k], sc)) << (8 * k);
-    *reinterpret_cast<uint2*>(codes + i) = make_uint2(lo, hi);
+    for (int u = 0; u < kQuantUnroll; ++u) {
+      const int64_t v = base + u * blockDim.x + threadIdx.x;
+      if (v >= nvec) continue;
+      const size_t i = (size_t)v * 8;
+      // Page slice of the vector (a slice is 2 D vectors, D a power of two).
+      const float sc = ssc[(uint32_t)(v >> vec_shift) % (uint32_t)n2];
+      float qv[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) qv[k] = __fdiv_rn(x[u][k], sc);
+      *reinterpret_cast<uint2*>(codes + i) =
+          make_uint2(e4m3x4_satrn(qv[0], qv[1], qv[2], qv[3]), e4m3x4_satrn(qv[4], qv[5], qv[6], qv[7]));
+    }
   }
 }
 
@@ -106,37 +122,40 @@ __device__ __forceinline__ int floor_log2_f32(float a) {
 __global__ void quant_mx_kernel(const void* src, int src_dtype, int64_t nelem, uint8_t* codes,
                                 uint8_t* scales) {
   const int64_t nvec = nelem / 8;
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t step = (int64_t)gridDim.x * blockDim.x * kQuantUnroll;
   // Warp-uniform trip count so the shuffles see the whole warp; the 4
   // threads of one 32-element block are always active together.
-  for (int64_t base = (int64_t)blockIdx.x * blockDim.x; base < nvec; base += stride) {
-    const int64_t v = base + threadIdx.x;
-    const bool act = v < nvec;
-    const size_t i = (size_t)(act ? v : 0) * 8;
-    float x[8];
-    load8(src, src_dtype, i, x);
-    float m = 0.f;
+  for (int64_t base = (int64_t)blockIdx.x * blockDim.x * kQuantUnroll; base < nvec; base += step) {
+    float x[kQuantUnroll][8];
 #pragma unroll
-    for (int k = 0; k < 8; ++k) m = fmaxf(m, fabsf(x[k]));
-    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
-    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
-    int e = m > 0.f ? floor_log2_f32(m) - 8 : -127;
-    if (e < -127) e = -127;
-    const float inv = __uint_as_float((uint32_t)(127 - e) << 23);  // 2^-e, a normal f32
-    uint32_t lo = 0, hi = 0;
+    for (int u = 0; u < kQuantUnroll; ++u) {
+      const int64_t v = base + u * blockDim.x + threadIdx.x;
+      load8(src, src_dtype, (size_t)(v < nvec ? v : 0) * 8, x[u]);
+    }
 #pragma unroll
-    for (int k = 0; k < 4; ++k) lo |= (uint32_t)float_to_e4m3_satrn(x[k] * inv) << (8 * k);
+    for (int u = 0; u < kQuantUnroll; ++u) {
+      const int64_t v = base + u * blockDim.x + threadIdx.x;
+      const size_t i = (size_t)(v < nvec ? v : 0) * 8;
+      float m = 0.f;
 #pragma unroll
-    for (int k = 0; k < 4; ++k) hi |= (uint32_t)float_to_e4m3_satrn(x[4 + k] * inv) << (8 * k);
-    if (!act) continue;
-    *reinterpret_cast<uint2*>(codes + i) = make_uint2(lo, hi);
-    if ((threadIdx.x & 3) == 0) scales[i / 32] = (uint8_t)(e + 127);
+      for (int k = 0; k < 8; ++k) m = fmaxf(m, fabsf(x[u][k]));
+      m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+      m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+      int e = m > 0.f ? floor_log2_f32(m) - 8 : -127;
+      if (e < -127) e = -127;
+      const float inv = __uint_as_float((uint32_t)(127 - e) << 23);  // 2^-e, a normal f32
+      const uint32_t lo = e4m3x4_satrn(x[u][0] * inv, x[u][1] * inv, x[u][2] * inv, x[u][3] * inv);
+      const uint32_t hi = e4m3x4_satrn(x[u][4] * inv, x[u][5] * inv, x[u][6] * inv, x[u][7] * inv);
+      if (v >= nvec) continue;
+      *reinterpret_cast<uint2*>(codes + i) = make_uint2(lo, hi);
+      if ((threadIdx.x & 3) == 0) scales[i / 32] = (uint8_t)(e + 127);
+    }
   }
 }
 
 __global__ void dequant_kernel(const uint8_t* codes, int format, const void* scales, int64_t nelem,
                                int Hkv, int D, void* dst, int dst_dtype) {
-  const int per = kPageSize * D;
+  const int vec_shift = 31 - __clz(kPageSize * D / 8);  // vectors per page slice = 2 D
   const int64_t nvec = nelem / 8;
   for (int64_t v = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; v < nvec;
        v += (int64_t)gridDim.x * blockDim.x) {
@@ -144,7 +163,7 @@ __global__ void dequant_kernel(const uint8_t* codes, int format, const void* sca
     const uint2 c = *reinterpret_cast<const uint2*>(codes + i);
     float sc;
     if (format == DD_DTYPE_E4M3)
-      sc = reinterpret_cast<const float*>(scales)[(i / per) % (2 * Hkv)];
+      sc = reinterpret_cast<const float*>(scales)[(uint32_t)(v >> vec_shift) % (uint32_t)(2 * Hkv)];
     else
       sc = e8m0_to_float(reinterpret_cast<const uint8_t*>(scales)[i / 32]);
     float y[8];
@@ -223,15 +242,17 @@ extern "C" int dd_quantize_kv_pages(const dd_quant_config* qc, const void* src, 
     if (e != cudaSuccess) return fail(DD_ERR_CUDA, cudaGetErrorString(e));
     const int64_t nslices = num_pages * 2 * Hkv;
     { ProfScope ps(kProfQuant, st);
-    amax_per_head_kernel<<<grid_for(nslices * 32, 256), 256, 0, st>>>(src, qc->src_dtype, nslices,
-                                                                       Hkv, D, amax); }
+    const int ga = grid_for(nslices * 32, 256);
+    if (D == 64) amax_per_head_kernel<64><<<ga, 256, 0, st>>>(src, qc->src_dtype, nslices, Hkv, amax);
+    else if (D == 128) amax_per_head_kernel<128><<<ga, 256, 0, st>>>(src, qc->src_dtype, nslices, Hkv, amax);
+    else amax_per_head_kernel<256><<<ga, 256, 0, st>>>(src, qc->src_dtype, nslices, Hkv, amax); }
     ProfScope ps(kProfQuant, st);
-    quant_e4m3_kernel<<<grid_for(nelem / 8, 256), 256, 0, st>>>(
+    quant_e4m3_kernel<<<grid_for(nelem / 8 / kQuantUnroll, 256), 256, 0, st>>>(
         src, qc->src_dtype, nelem, Hkv, D, amax, qc->scale_mode, codes,
         reinterpret_cast<float*>(scales));
   } else {
     ProfScope ps(kProfQuant, st);
-    quant_mx_kernel<<<grid_for(nelem / 8, 256), 256, 0, st>>>(src, qc->src_dtype, nelem, codes,
+    quant_mx_kernel<<<grid_for(nelem / 8 / kQuantUnroll, 256), 256, 0, st>>>(src, qc->src_dtype, nelem, codes,
                                                               reinterpret_cast<uint8_t*>(scales));
   }
   const cudaError_t e = cudaGetLastError();
