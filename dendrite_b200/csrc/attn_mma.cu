@@ -38,8 +38,7 @@
 namespace dd {
 
 constexpr int kMmaRows = 16;       // query rows per work item
-constexpr int kStreams = 4;        // consumer warps = independent streams
-constexpr int kMmaThreads = 2 * kStreams * 32;  // consumer warps, then producer warps
+constexpr int kStreams = 4;        // independent streams per CTA
 constexpr int kStepPages = 2;      // pages per stage
 constexpr int kItemSlots = 2;      // item descriptors per stream
 
@@ -52,7 +51,7 @@ struct MmaCfg {
   static constexpr int kMxBytes = KV == kKvMx ? kPageSize * (D / 32) : 0;
   // Stages are read in place by the consumer; FP8 stages are a quarter (E4M3)
   // of the bf16 ones, so the FP8 rings are deeper for the same bytes in flight.
-  static constexpr int kStages = KV == kKvBf16 ? 3 : 6;
+  static constexpr int kStages = KV == kKvBf16 ? 3 : 5;
   static constexpr int kRawStage = 2 * kStepPages * kSliceRaw;         // K0 K1 V0 V1
   static constexpr int kMxStage = 2 * kStepPages * kMxBytes;
   static constexpr int kStageAll = kRawStage;                          // 1 KiB multiple (swizzle)
@@ -60,7 +59,15 @@ struct MmaCfg {
   static constexpr int kQRowBytes = D * 2 + 16;                        // padded: conflict-free ldmatrix
   static constexpr int kQBytes = ((kMmaRows * kQRowBytes + 1023) / 1024) * 1024;
   static constexpr int kStreamBytes = ((kStages * kStageAll + kExpBytes + kQBytes + 1023) / 1024) * 1024;
-  static constexpr int kSmemBytes = kStreams * kStreamBytes + 1024;   // + alignment slack
+  // FP8 streams have two consumer warps (the widening makes a consumer warp
+  // issue-bound): consumer h takes page h of each stage, and at the end of an
+  // item consumer 1 hands its softmax state to consumer 0 through kXBytes of
+  // shared memory (68 floats per lane).
+  static constexpr bool kPair = KV != kKvBf16;
+  static constexpr int kConsumers = kPair ? 2 * kStreams : kStreams;
+  static constexpr int kThreads = (kConsumers + kStreams) * 32;  // consumers, then producers
+  static constexpr int kXBytes = kPair ? 68 * 32 * 4 : 0;
+  static constexpr int kSmemBytes = kStreams * (kStreamBytes + kXBytes) + 1024;   // + alignment slack
 };
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
@@ -133,12 +140,13 @@ struct StreamShared {
   uint64_t full[kMaxStages];
   uint64_t empty[kMaxStages];
   uint64_t q_empty;
+  uint64_t x_full, x_empty;  // FP8 consumer pairs: state handed over / read
   StageMeta meta[kMaxStages];
   WorkItem items[kItemSlots];
 };
 
 template <int D, int KV>
-__global__ void __launch_bounds__(kMmaThreads, 1)
+__global__ void __launch_bounds__(MmaCfg<D, KV>::kThreads, 1)
     attn_mma_kernel(const __grid_constant__ CUtensorMap kv_map, AttnArgs a) {
   using C = MmaCfg<D, KV>;
   static_assert(KV == kKvBf16 || D == 128, "FP8 fragments are laid out for head_dim 128");
@@ -148,30 +156,42 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
   __shared__ int abort_flag;
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
 
+  constexpr int kCons = C::kConsumers;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x < kStreams) {
     StreamShared& s = ss[threadIdx.x];
     for (int i = 0; i < S; ++i) {
       mbar_init(&s.full[i], 1);
-      mbar_init(&s.empty[i], 1);
+      mbar_init(&s.empty[i], C::kPair ? 2 : 1);
     }
-    mbar_init(&s.q_empty, 1);
+    mbar_init(&s.q_empty, C::kPair ? 2 : 1);
+    mbar_init(&s.x_full, 1);
+    mbar_init(&s.x_empty, 1);
   }
   if (threadIdx.x == 0) {
     abort_flag = 0;
     fence_mbar_init();
   }
-  if (threadIdx.x == kStreams * 32) prefetch_tmap(&kv_map);
+  if (threadIdx.x == kCons * 32) prefetch_tmap(&kv_map);
   __syncthreads();
+  if (C::kPair) {
+    // 384 threads launch at 168 registers (64,512); the producer warpgroup
+    // gives up to 56 and the two consumer warpgroups take 224:
+    // 128 x 56 + 256 x 224 = 64,512.
+    if (warp >= kCons)
+      asm volatile("setmaxnreg.dec.sync.aligned.u32 56;\n" ::: "memory");
+    else
+      asm volatile("setmaxnreg.inc.sync.aligned.u32 224;\n" ::: "memory");
+  }
 
-  if (warp >= kStreams) {
+  if (warp >= kCons) {
     // ------------------------------------------------------------ producer
     // Producer warp kStreams + c drives stream c with all 32 lanes, so a
     // stall on one stream's reads never delays another stream. Lane l holds
     // the id of page chunk_base + l of the current item (and of the next
     // 32-page chunk), read 32 at a time one chunk ahead, so a stage issues no
     // dependent global read; lanes issue the stage's copies in parallel.
-    const int c = warp - kStreams;
+    const int c = warp - kCons;
     StreamShared& sh = ss[c];
     uint8_t* base = smem + c * C::kStreamBytes;
     uint8_t* qbuf = base + S * C::kStageAll + C::kExpBytes;
@@ -371,8 +391,11 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
     (void)t_pf; (void)t_empty; (void)t_qe; (void)t_life;
   } else {
     // ------------------------------------------------------------ consumer
-    StreamShared& sh = ss[warp];
-    uint8_t* base = smem + warp * C::kStreamBytes;
+    const int cs = warp % kStreams, half = C::kPair ? warp / kStreams : 0;
+    StreamShared& sh = ss[cs];
+    uint8_t* base = smem + cs * C::kStreamBytes;
+    float* xbuf = reinterpret_cast<float*>(smem + kStreams * C::kStreamBytes + cs * C::kXBytes);
+    int pair_items = 0;  // items handed over (consumer 1) / taken over (consumer 0)
     uint8_t* qbuf = base + S * C::kStageAll + C::kExpBytes;
     WorkItem it{};
     uint32_t qa[D / 16][4];
@@ -441,8 +464,11 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
       const uint8_t* st = base + s * C::kStageAll;
       const uint8_t* kb;
       const uint8_t* vb;
-      kb = st;
-      vb = st + kStepPages * C::kSliceRaw;
+      // A consumer pair splits the stage: consumer h takes page pj = h as
+      // its page 0 (and no page 1).
+      const int pj = C::kPair ? half : 0;
+      kb = st + pj * C::kSliceRaw;
+      vb = st + (kStepPages + pj) * C::kSliceRaw;
       // Valid tokens per page of the step (0 = absent or skipped).
       int valid[2];
 #pragma unroll
@@ -453,6 +479,10 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
         valid[j] = 0;  // data-movement ceiling experiment only
 #endif
       }
+      if (C::kPair) {
+        valid[0] = valid[half];
+        valid[1] = 0;
+      }
       // MXFP8 exponent words of the stage, read before any code is widened:
       // kex[nt] = the four 32-dim blocks of K token nt*8 + lane/4, vex[j][i]
       // = those of V token 2c, 2c+1, 2c+8, 2c+9 (c = lane % 4) of page j.
@@ -460,15 +490,15 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
       if (KV == kKvMx) {
         const uint8_t* mx = base + S * C::kStageAll + s * C::kMxStage;
 #pragma unroll
-        for (int nt = 0; nt < 4; ++nt)
-          kex[nt] = *reinterpret_cast<const uint32_t*>(mx + (nt >> 1) * C::kMxBytes +
+        for (int nt = 0; nt < (C::kPair ? 2 : 4); ++nt)
+          kex[nt] = *reinterpret_cast<const uint32_t*>(mx + (pj + (nt >> 1)) * C::kMxBytes +
                                                         ((nt & 1) * 8 + (lane >> 2)) * (D / 32));
 #pragma unroll
-        for (int j = 0; j < 2; ++j)
+        for (int j = 0; j < (C::kPair ? 1 : 2); ++j)
 #pragma unroll
           for (int i = 0; i < 4; ++i)
             vex[j][i] = *reinterpret_cast<const uint32_t*>(
-                mx + (kStepPages + j) * C::kMxBytes + (2 * (lane & 3) + (i & 1) + 8 * (i >> 1)) * (D / 32));
+                mx + (kStepPages + pj + j) * C::kMxBytes + (2 * (lane & 3) + (i & 1) + 8 * (i >> 1)) * (D / 32));
       }
       if (valid[0] + valid[1] > 0) {
         // S = Q K^T for 16 rows x 32 tokens: four independent n-tile chains.
@@ -534,7 +564,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
           const int tok = (nt & 1) * 8 + tc;
           // Causal plans: token index within the node (items start at its
           // first token) against each row's limit.
-          const int abs0 = (m.page0 + (nt >> 1)) * kPageSize + tok;
+          const int abs0 = (m.page0 + pj + (nt >> 1)) * kPageSize + tok;
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
             const bool ok = tok + (c & 1) < vj && abs0 + (c & 1) < (c < 2 ? lim0 : lim1);
@@ -634,6 +664,44 @@ __global__ void __launch_bounds__(kMmaThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&sh.empty[s]);
       if (m.flags & kLast) {
+        if (C::kPair) {
+          // Consumer 1 hands its (m, l, o) over; consumer 0 merges it into its
+          // own (same fragment layout: lane-for-lane) and writes the state.
+          if (half == 1) {
+            if (pair_items > 0 && !mbar_wait(&sh.x_empty, (pair_items - 1) & 1, &abort_flag, a.err)) break;
+#pragma unroll
+            for (int n = 0; n < D / 8; ++n)
+#pragma unroll
+              for (int c = 0; c < 4; ++c) xbuf[(n * 4 + c) * 32 + lane] = o[n][c];
+            xbuf[64 * 32 + lane] = m0;
+            xbuf[65 * 32 + lane] = m1;
+            xbuf[66 * 32 + lane] = l0;
+            xbuf[67 * 32 + lane] = l1;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sh.x_full);
+            ++pair_items;
+            continue;
+          }
+          if (!mbar_wait(&sh.x_full, pair_items & 1, &abort_flag, a.err)) break;
+          const float pm0 = xbuf[64 * 32 + lane], pm1 = xbuf[65 * 32 + lane];
+          const float M0 = fmaxf(m0, pm0), M1 = fmaxf(m1, pm1);
+          const float fa0 = M0 == -INFINITY ? 0.f : fast_exp2(m0 - M0);
+          const float fb0 = M0 == -INFINITY ? 0.f : fast_exp2(pm0 - M0);
+          const float fa1 = M1 == -INFINITY ? 0.f : fast_exp2(m1 - M1);
+          const float fb1 = M1 == -INFINITY ? 0.f : fast_exp2(pm1 - M1);
+#pragma unroll
+          for (int n = 0; n < D / 8; ++n)
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+              o[n][c] = o[n][c] * (c < 2 ? fa0 : fa1) + xbuf[(n * 4 + c) * 32 + lane] * (c < 2 ? fb0 : fb1);
+          l0 = l0 * fa0 + xbuf[66 * 32 + lane] * fb0;
+          l1 = l1 * fa1 + xbuf[67 * 32 + lane] * fb1;
+          m0 = M0;
+          m1 = M1;
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&sh.x_empty);
+          ++pair_items;
+        }
         // Normalised partial state per row, written from registers.
         float L0 = l0 + __shfl_xor_sync(0xffffffffu, l0, 1);
         L0 += __shfl_xor_sync(0xffffffffu, L0, 2);
@@ -748,7 +816,7 @@ static cudaError_t launch_mma_t(const CUtensorMap& map, const AttnArgs& a, cudaS
   int dev = 0, sms = 148, per_sm = 1;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, attn_mma_kernel<D, KV>, kMmaThreads, smem);
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, attn_mma_kernel<D, KV>, MmaCfg<D, KV>::kThreads, smem);
   if (e != cudaSuccess) return e;
   const int ctas_needed = (a.num_items + kStreams - 1) / kStreams;
   int grid = std::max(1, std::min(ctas_needed, sms * std::max(per_sm, 1)));
@@ -757,7 +825,7 @@ static cudaError_t launch_mma_t(const CUtensorMap& map, const AttnArgs& a, cudaS
 #endif
   {
     ProfScope ps(kProfMma, st);
-    attn_mma_kernel<D, KV><<<grid, kMmaThreads, smem, st>>>(map, a);
+    attn_mma_kernel<D, KV><<<grid, MmaCfg<D, KV>::kThreads, smem, st>>>(map, a);
   }
   return cudaGetLastError();
 }
