@@ -1,6 +1,9 @@
 // C-ABI entry points: plan upload, cascade decode, flat paged decode, KV
 // append, head-shard scatter. Kernel selection lives here; the kernels are in
-// attn_simple.cu, attn_mma.cu, attn_tc.cu and merge.cu.
+// attn_simple.cu, attn_mma.cu, attn_tc.cu, attn_tc2.cu (CTA pairs, opt-in),
+// attn_tcs.cu (experiment builds only) and merge.cu; the planner is in
+// planner.cpp, the quantizer in quant.cu, batched appends and page copies in
+// append.cu, the head all-gather in collective.cu.
 #include <algorithm>
 #include <cmath>
 #include <cstring>

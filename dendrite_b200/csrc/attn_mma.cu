@@ -3,30 +3,36 @@
 // cut into 16-row items), bf16 / E4M3 / MXFP8 KV.
 //
 // Persistent, multi-stream kernel. One CTA per SM holds kStreams independent
-// streams; each stream is one consumer warp with its own ring of shared-
-// memory stages. Work items are claimed from a device counter (items are
-// sorted longest first), one item at a time per stream.
-//  - One producer warp serves all streams: lane c drives stream c. For the
-//    stream's current item it claims work, reads page ids a stage ahead, and
-//    fills free stages with TMA (cp.async.bulk.tensor): one box per 16-token
-//    page slice of K or of V ([16][head_dim] contiguous in the pool, 128-byte
-//    swizzle), plus a bulk copy of the item's query rows into the stream's Q
-//    buffer. Several streams per SM keep enough independent loads in flight
-//    to run HBM near its random-read ceiling.
+// streams, each with its own ring of shared-memory stages, one producer warp
+// and one consumer warp (bf16) or two (FP8). Work items are claimed from a
+// device counter (items are sorted longest first), one item at a time per
+// stream.
+//  - The stream's producer warp claims work, reads page ids a chunk ahead
+//    (32 at a time, one per lane) and fills free stages with TMA
+//    (cp.async.bulk.tensor), its lanes issuing a stage's copies in parallel:
+//    one box per 16-token page slice of K or of V ([16][head_dim] contiguous
+//    in the pool, 128-byte swizzle), plus a bulk copy of the item's query
+//    rows into the stream's Q buffer. Pages read by one item only stream
+//    L2 evict-first. Four streams per SM keep enough independent loads in
+//    flight to run HBM near its random-read ceiling.
 //  - FP8 pages land as 1-byte codes (+ E8M0 bytes for MXFP8) and stay FP8 in
-//    shared memory: the consumer widens them (code * scale rounded to bf16)
-//    straight into its mma fragments. Q.K^T contracts head dims in an order
+//    shared memory: the consumers widen them (code * scale rounded to bf16)
+//    straight into their mma fragments. Q.K^T contracts head dims in an order
 //    where a lane's four K codes per k-step are one 4-byte word (Q is loaded
 //    in the same order); for P.V a lane reads one word per token of four
 //    tokens, transposes the 4x4 bytes and widens each head dim's four codes,
-//    and the epilogue puts the head dims back in order. With no bf16 copy of
-//    a stage, the rings hold 5-6 FP8 stages, the same bytes in flight as bf16.
-//  - The consumer warp owns all 16 query rows of its item (a GQA group of one
-//    or more queries sharing the node). Per stage it takes two pages (32
-//    tokens): q.k^T and p.v as m16n8k16 bf16 tensor-core tiles with f32
-//    accumulators, online softmax in the log2 domain, P split into two bf16
-//    terms so P.V keeps ~16 significant bits of P. At the end of the item it
-//    writes one normalised partial state per row straight from registers.
+//    and the epilogue puts the head dims back in order. Widening makes a
+//    consumer warp issue-bound, so FP8 streams have two: consumer h takes
+//    page h of each stage, and consumer 1 hands its softmax state to
+//    consumer 0 at the end of an item.
+//  - A consumer owns all 16 query rows of its item (a GQA group of one or
+//    more queries sharing the node). Per stage it takes two pages (32
+//    tokens; one page each for an FP8 pair): q.k^T and p.v as m16n8k16 bf16
+//    tensor-core tiles with f32 accumulators, online softmax in the log2
+//    domain, P split into two bf16 terms so P.V keeps ~16 significant bits
+//    of P. At the end of the item it writes one normalised partial state per
+//    row straight from registers. Causal (prefill) items mask each row's
+//    scores past its query's token limit.
 // All waits are bounded mbarrier waits; a timeout sets an error word.
 // The arithmetic is ReferenceBackend::decode's
 // (crates/dendrite-core/src/attention/backend.rs:254-262) over the node's

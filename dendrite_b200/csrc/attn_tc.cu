@@ -9,7 +9,7 @@
 //               of [16 tokens][64 dims], 128-byte swizzle) into the K/V
 //               ring; lane p owns page p of each tile and reads its id one
 //               tile ahead. FP8 pages go to a staging ring instead and warps
-//               10-11 widen them to bf16 in the ring's layout.
+//               10-13 widen them to bf16 in the ring's layout.
 //   warp 1      allocates all 512 TMEM columns; lane 0 issues every
 //               tcgen05.mma and signals completion with tcgen05.commit, per
 //               tile j in the order
@@ -32,6 +32,9 @@
 // a rescale. Each tcgen05.mma (M = N = 128, K = 16) occupies the tensor
 // pipe ~90 cycles, so a 256-row tile keeps it busy for 48 of them per
 // 128 tokens while each sub-tile's softmax has the other's 24 to run in.
+//
+// Causal (prefill) items mask each row's scores past its query's token
+// limit in the softmax; their products still cover the item's tokens.
 //
 // The arithmetic is ReferenceBackend::decode's
 // (crates/dendrite-core/src/attention/backend.rs:254-262) over the node's
