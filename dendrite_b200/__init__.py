@@ -12,6 +12,6 @@ from .backend import (PAGE_SIZE, SUPPORTED_HEAD_DIMS, AttentionConfig, B200Backe
                       BlockTable, CascadePlan, append_kv_batch, cascade_decode, copy_pages,
                       decode_paged, dequantize_kv_pages,
                       make_config, merge_states, quantize_kv_pages, scatter_head_shards,
-                      workspace_status)
+                      selftest_wait, workspace_status)
 
 __version__ = "0.1.0"

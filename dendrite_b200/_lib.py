@@ -100,6 +100,7 @@ SIGNATURES = {
     "dd_plan_destroy": (None, [_VP]),
     "dd_plan_rebuild": (C.c_int, [C.c_void_p, C.c_int32, _I32P, _U32P, _I32P]),
     "dd_plan_advance": (C.c_int, [C.c_void_p, _I32P, _U32P]),
+    "dd_selftest_wait": (C.c_int, [_VP, C.c_uint64, _VP]),
     "dd_plan_get_info": (C.c_int, [_VP, C.POINTER(PlanInfo)]),
     "dd_plan_upload": (C.c_int, [_VP, _VP, C.c_size_t, _VP]),
     "dd_plan_export_nodes": (C.c_int, [_VP, _I32P, _I32P, _I32P, _I32P, _I32P, _I32P, _U32P,

@@ -298,6 +298,12 @@ def workspace_status(workspace: torch.Tensor, stream=None) -> tuple[int, int]:
     return code.value, aux.value
 
 
+def selftest_wait(workspace: torch.Tensor, limit_ns: int, stream=None) -> None:
+    """Run the kernels' bounded wait out on purpose (dd_selftest_wait): the
+    workspace then reports a wait timeout (status code 2)."""
+    check(lib.dd_selftest_wait(_ptr(workspace), int(limit_ns), _stream(stream)), "dd_selftest_wait")
+
+
 def merge_states(o_a, lse_a, o_b, lse_b, stream=None):
     """Batched merge_attention_outputs (cascade.rs:116-124) on the GPU."""
     n, D = o_a.shape[0], o_a.shape[-1]

@@ -114,9 +114,34 @@ __global__ void copy_pages_kernel(int32_t n, int num_pages, size_t page_bytes, s
   }
 }
 
+// The kernels' bounded wait, run out on purpose: an mbarrier that nothing
+// arrives on, waited for with limit_ns; the wait gives up, records
+// kDevErrWaitTimeout in the workspace header and the kernel returns.
+__global__ void selftest_wait_kernel(WsHeader* err, uint64_t limit_ns) {
+  __shared__ uint64_t bar;
+  __shared__ int abort;
+  mbar_init(&bar, 1);
+  abort = 0;
+  fence_mbar_init();
+  mbar_wait_limit(&bar, 0, &abort, err, limit_ns);
+}
+
 }  // namespace dd
 
 using namespace dd;
+
+extern "C" int dd_selftest_wait(void* workspace, uint64_t limit_ns, dd_stream_t stream) {
+  if (!workspace) return fail(DD_ERR_INVALID_ARGUMENT, "workspace is NULL");
+  if (limit_ns == 0 || limit_ns > kWaitLimitNs) return fail(DD_ERR_INVALID_ARGUMENT, "limit_ns must be in (0, 2 s]");
+  cudaStream_t st = (cudaStream_t)stream;
+  cudaError_t e = cudaMemsetAsync(workspace, 0, kWsHeaderBytes, st);
+  if (e == cudaSuccess) {
+    selftest_wait_kernel<<<1, 1, 0, st>>>(reinterpret_cast<WsHeader*>(workspace), limit_ns);
+    e = cudaGetLastError();
+  }
+  if (e != cudaSuccess) return fail(DD_ERR_CUDA, std::string("selftest_wait: ") + cudaGetErrorString(e));
+  return DD_OK;
+}
 
 extern "C" int dd_append_kv_batch(const dd_attn_config* cfg, void* kv_pages, void* kv_scales,
                                   int32_t n, const uint32_t* page_ids, const int32_t* slots,

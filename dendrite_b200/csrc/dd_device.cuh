@@ -203,23 +203,28 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait: returns false (and sets *abort) if the phase does not
-// complete within kWaitLimitNs, or immediately if *abort is already set.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
-                                          WsHeader* err) {
+// Bounded wait: returns false (and sets *abort, and the workspace error
+// word) if the phase does not complete within limit_ns, or immediately if
+// *abort is already set.
+__device__ __forceinline__ bool mbar_wait_limit(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                                WsHeader* err, uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_ns();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((it & 255u) == 0) {
       if (*abort) return false;
-      if (global_ns() - t0 > kWaitLimitNs) {
+      if (global_ns() - t0 > limit_ns) {
         *abort = 1;
         report_error(err, kDevErrWaitTimeout, 0);
         return false;
       }
     }
   }
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                          WsHeader* err) {
+  return mbar_wait_limit(bar, parity, abort, err, kWaitLimitNs);
 }
 
 // ----------------------------------------------------------------------- TMA

@@ -236,6 +236,14 @@ int dd_decode_paged(const dd_attn_config* cfg, int32_t batch_size, int32_t max_p
  * backend.rs:228-234; aux = the id); 2 = a kernel's bounded wait timed out. */
 int dd_workspace_status(const void* workspace, dd_stream_t stream, uint32_t* code, uint32_t* aux);
 
+/* Failure-path self-test: runs the kernels' bounded mbarrier wait on a
+ * barrier nothing arrives on, with limit_ns (<= 2 s) instead of 2 s. The
+ * kernel gives up, records status code 2 (a bounded wait timed out) in the
+ * workspace header (>= 256 bytes; read with dd_workspace_status) and
+ * returns: the context stays
+ * usable. For tests of the failure detection. */
+int dd_selftest_wait(void* workspace, uint64_t limit_ns, dd_stream_t stream);
+
 /* 1 when the tcgen05 (TMEM) kernel for wide shared nodes is compiled in. */
 int dd_tc_available(void);
 
