@@ -68,3 +68,18 @@ def test_advance_rejects_bad_input():
         plan.advance([1], [99])          # block id >= num_pages
     pf = dd.CascadePlan.prefill(cfg, [0, 1], [0], [0], [5])
     assert not pf.advance([1] * 5, [0] * 5)
+
+
+def test_advance_without_tokens_keeps_the_plan():
+    tb = wl.small_tree(5, Hq=8, Hkv=2, D=128)
+    cfg = dd.make_config(8, 2, 128, tb.num_pages)
+    plan = dd.CascadePlan(cfg, tb.indptr, tb.block_ids, tb.num_tokens)
+    before = (_node_set(plan), plan.info().kv_tokens)
+    assert plan.advance(np.zeros(tb.batch_size, np.int32))
+    assert (_node_set(plan), plan.info().kv_tokens) == before
+
+
+def test_advance_refuses_flat_plans():
+    cfg = dd.make_config(8, 2, 128, 64)
+    plan = dd.CascadePlan(cfg, [0, 2, 4], [0, 1, 2, 3], [20, 30], share_prefixes=False)
+    assert not plan.advance([1, 1], [5, 6])

@@ -92,3 +92,14 @@ def test_prefill_plan_rejects_bad_input():
         dd.CascadePlan.prefill(cfg, [0, 1], [99], [0], [5])       # block id >= num_pages
     with pytest.raises(dd.InvalidArgument):
         dd.CascadePlan.prefill(cfg, [0, 1], [0], [-1], [5])
+
+
+def test_prefill_plan_skips_sequences_without_new_tokens():
+    cfg = dd.make_config(8, 2, 128, 64)
+    p = dd.CascadePlan.prefill(cfg, [0, 2, 4, 6], np.arange(6), [20, 17, 5], [0, 9, 0])
+    info = p.info()
+    assert info.batch_size == 9
+    n = p.nodes()
+    assert int(n["num_q"].max()) == 9 and sorted(n["query_order"]) == list(range(9))
+    empty = dd.CascadePlan.prefill(cfg, [0, 1], [0], [10], [0])
+    assert empty.info().batch_size == 0 and empty.info().num_items == 0
