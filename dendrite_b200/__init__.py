@@ -14,4 +14,6 @@ from .backend import (PAGE_SIZE, SUPPORTED_HEAD_DIMS, AttentionConfig, B200Backe
                       make_config, merge_states, quantize_kv_pages, scatter_head_shards,
                       selftest_wait, workspace_status)
 
+from .paged_cache import PagedKVCache  # noqa: F401
+
 __version__ = "0.1.0"
