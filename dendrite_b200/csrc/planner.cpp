@@ -734,6 +734,8 @@ int dd_plan_advance(dd_plan* p, const int32_t* tokens_added, const uint32_t* new
     const int32_t leaf = p->q_leaf[pos[b]];
     if (leaf < 0 || p->nodes[leaf].num_q != 1)
       return fail(DD_ERR_NOT_AVAILABLE, "query " + std::to_string(b) + " shares its last pages; re-plan");
+    if (p->nodes[leaf].kind == kItemTcs)  // grouped items are reordered after the build
+      return fail(DD_ERR_NOT_AVAILABLE, "streaming-group items are not advanced; re-plan");
     if (p->nodes[leaf].last_valid == kPageSize) {
       if (!new_block) return fail(DD_ERR_INVALID_ARGUMENT, "new_block is NULL");
       if (new_block[b] >= (uint32_t)p->cfg.num_pages)
