@@ -184,7 +184,8 @@ int dd_plan_rebuild(dd_plan* plan, int32_t batch_size, const int32_t* block_indp
  * starts a new block went to block new_block[b] (read only for those). In
  * place only for queries that own their last pages (a leaf of the plan's
  * tree with no other query): their nodes gain the token / block and their
- * items are re-cut; the device image must be uploaded again. Returns
+ * items are re-cut; the device image must be uploaded again (its size,
+ * dd_plan_get_info().device_bytes, can grow by the moved page runs). Returns
  * DD_ERR_NOT_AVAILABLE, with the plan unchanged, when some query shares its
  * last pages (a fresh fork, a copy-on-write pending), for prefill and flat
  * plans, or when the page list needs compacting: the caller then re-plans
