@@ -384,7 +384,8 @@ static void build_items(dd_plan* p) {
   }
   p->path_slots.resize(p->path_indptr[B]);
   sc.qcursor.assign(p->path_indptr.begin(), p->path_indptr.end() - 1);
-  for (int k = 0; k < kNumItemKinds; ++k) p->items[k].reserve(n_items[k]);
+  for (int k = 0; k < kNumItemKinds; ++k) p->items[k].resize(n_items[k]);
+  int64_t item_fill[kNumItemKinds] = {0, 0, 0, 0, 0};
   // Pass 2: path slots, in DFS order.
   for (size_t ni = 0; ni < N; ++ni) {
     const Node& n = p->nodes[ni];
@@ -408,8 +409,10 @@ static void build_items(dd_plan* p) {
     const int32_t k = sc.node_k[ni];
     n.kind = kind;
     n.k = k;
-    n.item_begin = (int32_t)p->items[kind].size();
+    n.item_begin = (int32_t)item_fill[kind];
     n.item_count = (int32_t)(k * Hkv * row_tiles);
+    WorkItem* out = p->items[kind].data() + item_fill[kind];
+    item_fill[kind] += n.item_count;
     for (int32_t ci = 0; ci < k; ++ci) {
       const int32_t pb = (int32_t)((int64_t)ci * n.page_count / k);
       const int32_t pe = (int32_t)((int64_t)(ci + 1) * n.page_count / k);
@@ -433,7 +436,7 @@ static void build_items(dd_plan* p) {
           if (kind == kItemMma && row_tiles == 1) it.nrows |= kItemSoleReader;
           it.q_begin = n.q_begin;
           it.slot_base = slot_base;
-          p->items[kind].push_back(it);
+          *out++ = it;
         }
     }
   }
