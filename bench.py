@@ -89,9 +89,25 @@ def dist_env():
     return world, rank, local
 
 
+def _workloads():
+    """dendrite_b200/workloads.py (pure numpy), loaded by path: importing it
+    through the package would load libdendrite_b200.so, which the reference
+    arm must not map."""
+    import importlib.util
+
+    name = "dendrite_b200_workloads_host"
+    if name in sys.modules:
+        return sys.modules[name]
+    spec = importlib.util.spec_from_file_location(name, ROOT / "dendrite_b200" / "workloads.py")
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
 def make_tree(name: str, rank: int, world: int):
     """This rank's tree batch and the job's total query count."""
-    from dendrite_b200 import workloads as wl
+    wl = _workloads()
 
     w = WORKLOADS[name]
     if w["tree"] == "prefill":
@@ -202,15 +218,19 @@ def oracle_threads(tb) -> int:
 
 def cpu_sample_rate(tb, pool, q_f32, budget_s: float, threads: int):
     """Reference CPU algorithm (oracle restatement of ReferenceBackend::decode_batch)
-    on the first queries of the batch; returns (queries/s, n queries, seconds)."""
+    on the first queries of the batch, its per-thread scratch allocated and
+    touched before the timed calls; returns (queries/s, n queries, seconds)."""
     import oracle
+
+    scratch = oracle.DecodeScratch(threads, tb.num_qo_heads, tb.num_kv_heads, tb.head_dim,
+                                   int(np.diff(tb.indptr).max()) * 16)
 
     def run(n):
         ip = tb.indptr[: n + 1]
         ids = tb.block_ids[: ip[-1]]
         t0 = time.perf_counter()
         oracle.decode_batch(q_f32[:n], pool, ip, ids, tb.num_tokens[:n], tb.num_kv_heads,
-                            threads=threads)
+                            scratch=scratch)
         return time.perf_counter() - t0
 
     n = min(threads, tb.batch_size)
@@ -297,12 +317,17 @@ def run_reference(args):
         pool = oracle.dequantize(codes, sc, w["kv"])
     q = oracle.bf16_bits_to_f32(qbits)
     threads = oracle_threads(tb)
-    n = min(tb.batch_size, threads)
+    # Each step is a bounded sample of the batch: 8 queries per thread (all
+    # of them when the batch is smaller), with every worker's gather / repeat
+    # scratch allocated and touched before the timed steps.
+    n = min(tb.batch_size, 8 * threads)
     ip = tb.indptr[: n + 1]
+    scratch = oracle.DecodeScratch(threads, tb.num_qo_heads, tb.num_kv_heads, tb.head_dim,
+                                   int(np.diff(ip).max()) * 16)
 
     def step():
         oracle.decode_batch(q[:n], pool, ip, tb.block_ids[: ip[-1]], tb.num_tokens[:n],
-                            tb.num_kv_heads, threads=threads)
+                            tb.num_kv_heads, scratch=scratch)
 
     for _ in range(args.warmup):
         step()
@@ -311,7 +336,8 @@ def run_reference(args):
         step()
     dt = time.perf_counter() - t0
     val = n * args.steps / dt
-    sample = f"first {n} of {tb.batch_size} queries per step ({threads} threads), {args.steps} steps"
+    sample = (f"first {n} of {tb.batch_size} queries per step ({threads} threads, scratch "
+              f"preallocated), {args.steps} steps")
     line = dict(base, metric=METRIC, value=val, unit="queries/s", ms_per_step=dt / args.steps * 1e3,
                 higher_is_better=True, dtype="f32",
                 cpu_baseline={"value": val, "unit": "queries/s", "cores": threads, "kind": "port",
@@ -343,7 +369,7 @@ def timed_steps(step, flush, args, world, rank, local, dev):
         uuids = [None] * world
         dist.all_gather_object(uuids, uuid)
     clocks = Clocks(",".join(uuids) if rank == 0 else None,
-                    ROOT / "gpurun_out" / "clocks.csv" if (ROOT / "gpurun_out").is_dir() else None)
+                    Path(args.clocks_csv) if args.clocks_csv else None)
     clocks.ready()
     if world > 1:
         dist.barrier()  # rank 0 waited for the sampler: start the timed steps together
@@ -703,6 +729,8 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="mcts8b")
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--clocks-csv", default=None,
+                    help="also write the raw nvidia-smi clock samples of the timed region here")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":

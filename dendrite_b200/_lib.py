@@ -112,6 +112,7 @@ SIGNATURES = {
     "dd_workspace_status": (C.c_int, [_VP, _VP, _U32P, _U32P]),
     "dd_decode_paged_static": (C.c_int, [_CFGP, C.c_int32, C.c_int32, _VP, _VP, _VP, _VP, _VP, _VP,
                                          _VP, _VP, _VP]),
+    "dd_decode_paged_static_status": (C.c_int, [_VP, _U32P, _U32P]),
     "dd_merge_states": (C.c_int, [C.c_int32, C.c_int32, _VP, _VP, _VP, _VP, _VP, _VP, _VP]),
     "dd_append_kv": (C.c_int, [_CFGP, _VP, C.c_uint32, C.c_int32, C.c_int32, _VP, _VP, _VP]),
     "dd_quantize_workspace_size": (C.c_size_t, [_QCP]),

@@ -1,7 +1,7 @@
 // C-ABI entry points: plan upload, cascade decode, flat paged decode, KV
 // append, head-shard scatter. Kernel selection lives here; the kernels are in
-// attn_simple.cu, attn_mma.cu, attn_tc.cu, attn_tc2.cu (CTA pairs, opt-in),
-// attn_tcs.cu (experiment builds only) and merge.cu; the planner is in
+// attn_simple.cu, attn_mma.cu, attn_tc.cu, attn_tc2.cu (CTA pairs, opt-in)
+// and merge.cu; the planner is in
 // planner.cpp, the quantizer in quant.cu, batched appends and page copies in
 // append.cu, the head all-gather in collective.cu.
 #include <algorithm>
@@ -16,8 +16,6 @@ int launch_attn_mma(const AttnArgs& a, int64_t num_pages, cudaStream_t st);
 bool mma_supported(int D, int kv_dtype);
 int launch_attn_tc(const AttnArgs& a, int64_t num_pages, int num_items, cudaStream_t st);
 int launch_attn_tc2(const AttnArgs& a, int64_t num_pages, int num_items, cudaStream_t st);
-int launch_attn_tcs(const AttnArgs& a, int64_t num_pages, const int32_t* groups, int num_groups,
-                    int max_ctas, cudaStream_t st);
 cudaError_t launch_merge(const MergeArgs& a, cudaStream_t st);
 
 static int cuda_fail(cudaError_t e, const char* what) {
@@ -169,11 +167,7 @@ extern "C" int dd_cascade_decode(const dd_attn_config* cfg, const dd_plan* p, co
     const int n = (int)p->items[k].size();
     if (!n || k == kItemTc || k == kItemTc2) continue;
     a.items = reinterpret_cast<const WorkItem*>(base + p->off_items[k]);
-    if (k == kItemTcs) {
-      const int ng = (int)(p->tcs_groups.size() / 4);
-      rc = launch_attn_tcs(a, cfg->num_pages, reinterpret_cast<const int32_t*>(base + p->off_groups), ng, 0, st);
-      if (rc) return rc;
-    } else if (k == kItemSimple) {
+    if (k == kItemSimple) {
       e = launch_attn_simple(a, dim3(n), st);
       if (e != cudaSuccess) return cuda_fail(e, "attn_simple launch");
     } else {

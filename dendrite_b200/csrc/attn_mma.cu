@@ -129,18 +129,6 @@ struct StageMeta {
 };
 enum { kFirst = 1, kLast = 2, kDone = 4 };
 
-// Cycle accounting for pipeline experiments (off unless DD_EXPERIMENT_TIMING).
-#ifdef DD_EXPERIMENT_TIMING
-#define DD_TSTART(v) const long long v = clock64();
-#define DD_TACC(acc, v) acc += clock64() - v;
-#define DD_TFLUSH(a, slot, acc) \
-  atomicAdd(reinterpret_cast<unsigned long long*>(&(a).err->pad[1]) + (slot), (unsigned long long)(acc));
-#else
-#define DD_TSTART(v)
-#define DD_TACC(acc, v)
-#define DD_TFLUSH(a, slot, acc)
-#endif
-
 constexpr int kMaxStages = 6;
 struct StreamShared {
   uint64_t full[kMaxStages];
@@ -246,16 +234,12 @@ __global__ void __launch_bounds__(MmaCfg<D, KV>::kThreads, 1)
     };
     const uint64_t pol_first = l2_policy(true), pol_normal = l2_policy(false);
     uint64_t pol = pol_normal;
-    long long t_pf = 0, t_empty = 0, t_qe = 0;
-    DD_TSTART(tlife)
     uint64_t t_idle = global_ns();
     while (!finished) {
       if (abort_flag) break;
       bool done = false;
       if (need_item) {
-        DD_TSTART(tpf)
         while (pf_state < kPfStates) pf_step();  // completes the prefetch (or all of it when disabled)
-        DD_TACC(t_pf, tpf)
         done = pf_idx >= a.num_items;
         if (!done) {
           it = pf_it;
@@ -272,7 +256,6 @@ __global__ void __launch_bounds__(MmaCfg<D, KV>::kThreads, 1)
       // Wait (bounded, non-blocking poll) for a free stage.
       const int s = stage_idx % S;
       if (stage_idx >= S) {
-        DD_TSTART(tem)
         bool ok = true;
         while (!mbar_try_wait(&sh.empty[s], ((stage_idx / S) - 1) & 1)) {
           if (global_ns() - t_idle > kWaitLimitNs) {
@@ -280,7 +263,6 @@ __global__ void __launch_bounds__(MmaCfg<D, KV>::kThreads, 1)
             break;
           }
         }
-        DD_TACC(t_empty, tem)
         if (!__all_sync(0xffffffffu, ok)) {
           if (lane == 0) {
             abort_flag = 1;
@@ -290,11 +272,9 @@ __global__ void __launch_bounds__(MmaCfg<D, KV>::kThreads, 1)
         }
       }
       // The Q buffer of the stream is reused once the consumer has read it.
-      DD_TSTART(tqe)
       if (need_item && !done && item_count >= 1 &&
           !__all_sync(0xffffffffu, mbar_wait(&sh.q_empty, (item_count - 1) & 1, &abort_flag, a.err)))
         break;
-      DD_TACC(t_qe, tqe)
       if (done) {
         if (lane == 0) {
           StageMeta m;
@@ -382,19 +362,8 @@ __global__ void __launch_bounds__(MmaCfg<D, KV>::kThreads, 1)
       }
       ++stage_idx;
       t_idle = global_ns();
-#ifndef DD_EXPERIMENT_NO_PREFETCH
       if (!finished && pf_state < kPfStates) pf_step();
-#endif
     }
-    long long t_life = 0;
-    DD_TACC(t_life, tlife)
-    if (lane == 0) {
-      DD_TFLUSH(a, 2, t_empty)
-      DD_TFLUSH(a, 3, t_life)
-      DD_TFLUSH(a, 4, t_qe)
-      DD_TFLUSH(a, 5, t_pf)
-    }
-    (void)t_pf; (void)t_empty; (void)t_qe; (void)t_life;
   } else {
     // ------------------------------------------------------------ consumer
     const int cs = warp % kStreams, half = C::kPair ? warp / kStreams : 0;
@@ -409,16 +378,11 @@ __global__ void __launch_bounds__(MmaCfg<D, KV>::kThreads, 1)
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
     float sc_k = 1.f, sc_v = 1.f;  // per-head E4M3 scales of the current item
     int lim0 = INT_MAX, lim1 = INT_MAX;  // causal plans: tokens seen by rows lane/4, +8
-    int items_started = 0;
-    long long t_full = 0;
-    DD_TSTART(tclife)
     const int tc = (lane & 3) * 2;
 
     for (int stage_idx = 0;; ++stage_idx) {
       const int s = stage_idx % S;
-      DD_TSTART(tfw)
       if (!mbar_wait(&sh.full[s], (stage_idx / S) & 1, &abort_flag, a.err)) break;
-      DD_TACC(t_full, tfw)
       const StageMeta m = sh.meta[s];
       if (m.flags & kDone) break;
       if (m.flags & kFirst) {
@@ -450,7 +414,6 @@ __global__ void __launch_bounds__(MmaCfg<D, KV>::kThreads, 1)
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&sh.q_empty);
-        ++items_started;
 #pragma unroll
         for (int n = 0; n < D / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
         m0 = m1 = -INFINITY;
@@ -481,9 +444,6 @@ __global__ void __launch_bounds__(MmaCfg<D, KV>::kThreads, 1)
       for (int j = 0; j < 2; ++j) {
         valid[j] = j < np ? ((m.page0 + j == it.npages - 1) ? it.last_valid : kPageSize) : 0;
         if ((m.invalid >> j) & 1) valid[j] = 0;
-#ifdef DD_EXPERIMENT_NO_COMPUTE
-        valid[j] = 0;  // data-movement ceiling experiment only
-#endif
       }
       if (C::kPair) {
         valid[0] = valid[half];
@@ -743,14 +703,6 @@ __global__ void __launch_bounds__(MmaCfg<D, KV>::kThreads, 1)
         }
       }
     }
-    long long t_clife = 0;
-    DD_TACC(t_clife, tclife)
-    if (lane == 0) {
-      DD_TFLUSH(a, 0, t_full)
-      DD_TFLUSH(a, 1, t_clife)
-      DD_TFLUSH(a, 6, items_started)
-    }
-    (void)t_full; (void)t_clife;
   }
   __syncthreads();
 }
@@ -826,9 +778,6 @@ static cudaError_t launch_mma_t(const CUtensorMap& map, const AttnArgs& a, cudaS
   if (e != cudaSuccess) return e;
   const int ctas_needed = (a.num_items + kStreams - 1) / kStreams;
   int grid = std::max(1, std::min(ctas_needed, sms * std::max(per_sm, 1)));
-#ifdef DD_EXPERIMENT_MMA_GRID
-  if (const char* g = getenv("DD_MMA_GRID")) grid = std::max(1, std::min(grid, atoi(g)));
-#endif
   {
     ProfScope ps(kProfMma, st);
     attn_mma_kernel<D, KV><<<grid, MmaCfg<D, KV>::kThreads, smem, st>>>(map, a);

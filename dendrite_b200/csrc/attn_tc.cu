@@ -63,28 +63,12 @@ constexpr int kTcConvWarps = 4;
 template <int KV>
 struct TcCfg {
   static constexpr bool kFp8 = KV != DD_DTYPE_BF16;
-#ifdef DD_EXPERIMENT_TC_SLOTS
-  static constexpr int kSlots = kFp8 ? 3 : DD_EXPERIMENT_TC_SLOTS;
-#else
   static constexpr int kSlots = kFp8 ? 3 : 4;    // K/V ring slots (32 KiB each)
-#endif
   static constexpr int kThreads = kFp8 ? 320 + 32 * kTcConvWarps : 320;
   static constexpr int kSmem =
       2 * kTcQBytes + kSlots * kTcSlotBytes + (kFp8 ? kTcStages * kTcStageBytes : 0) + 1024;
 };
 constexpr int kTcMaxSlots = 5;
-// Wait-time and phase counters for pipeline experiments (compiled in only
-// with DD_EXPERIMENT_TIMING; summed into the workspace header's pad words).
-#ifdef DD_EXPERIMENT_TIMING
-#define TCW(slot, expr) ([&]() { const long long _t0 = clock64(); const bool _r = (expr); \
-                                 tacc[slot] += clock64() - _t0; return _r; }())
-#define TCP_START(v) long long v = clock64();
-#define TCP_MARK(slot, v) { const long long _n = clock64(); tacc2[slot] += _n - v; v = _n; }
-#else
-#define TCW(slot, expr) (expr)
-#define TCP_START(v)
-#define TCP_MARK(slot, v)
-#endif
 
 struct TcBars {
   uint64_t kv_full[kTcMaxSlots];
@@ -120,11 +104,6 @@ __global__ void __launch_bounds__(TcCfg<KV>::kThreads, 1)
   const int ntiles = (npages + kTcPagesPerTile - 1) / kTcPagesPerTile;
   const bool has_b = it.nrows > 128;  // second sub-tile in use
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-#ifdef DD_EXPERIMENT_TIMING
-  long long tacc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-  long long tacc2[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-  const long long t_entry = clock64();
-#endif
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kTcSlots; ++s) {
@@ -156,9 +135,6 @@ __global__ void __launch_bounds__(TcCfg<KV>::kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = bars.tmem_base;
-#ifdef DD_EXPERIMENT_TIMING
-  if (threadIdx.x == 64) tacc2[5] += clock64() - t_entry;  // setup: barriers, TMEM alloc
-#endif
   volatile int* abort = &bars.abort;
 
   if (warp == 0) {
@@ -218,7 +194,7 @@ __global__ void __launch_bounds__(TcCfg<KV>::kThreads, 1)
         nxt = pn < npages ? pages[pn] : 0xFFFFFFFFu;
       }
       if (idx >= kTcSlots &&
-          !TCW(6, mbar_wait(&bars.kv_empty[s], ((idx / kTcSlots) - 1) & 1, abort, a.err)))
+          !(mbar_wait(&bars.kv_empty[s], ((idx / kTcSlots) - 1) & 1, abort, a.err)))
         break;
       if (lane == 0) mbar_arrive_expect_tx(&bars.kv_full[s], kTcSlotBytes);
       __syncwarp();
@@ -273,23 +249,19 @@ __global__ void __launch_bounds__(TcCfg<KV>::kThreads, 1)
         const int sv = (2 * j + 1) % kTcSlots;
         const uint64_t vd = v_desc0 + (uint64_t)((sv * kTcSlotBytes) >> 4);
         for (int x = 0; ok && x < nsub; ++x) {
-          if (!TCW(4 - x, mbar_wait(&bars.p_full[x], j & 1, abort, a.err))) { ok = false; break; }
-          if (x == 0 && !TCW(5, wait_slot(2 * j + 1))) { ok = false; break; }
+          if (!(mbar_wait(&bars.p_full[x], j & 1, abort, a.err))) { ok = false; break; }
+          if (x == 0 && !(wait_slot(2 * j + 1))) { ok = false; break; }
           tc_fence_after();
           const uint32_t d = tbase + col_o(x);
 #pragma unroll
-#ifdef DD_EXPERIMENT_NO_SPLIT
-          for (int st = 0; st < 8; ++st) {
-#else
           for (int st = 0; st < 16; ++st) {
-#endif
             const int kt = st & 7, part = st >> 3;  // hi terms, then lo terms
             const uint32_t pa = tbase + col_s(x) + (kt >> 2) * 64 + part * 32 + (kt & 3) * 8;
             umma_ts(d, pa, vd + (uint64_t)((kt * 2048) >> 4), kIdescPV, (j > 0 || st > 0) ? 1u : 0u);
           }
           if (j + 1 < ntiles) {
             if (x == 0) {
-              if (!TCW(2, wait_slot(2 * j + 2))) { ok = false; break; }
+              if (!(wait_slot(2 * j + 2))) { ok = false; break; }
               tc_fence_after();
             }
             issue_qk(x, j + 1);
@@ -370,9 +342,6 @@ __global__ void __launch_bounds__(TcCfg<KV>::kThreads, 1)
       }
       fence_proxy_async_smem();
       mbar_arrive(&bars.q_ready);
-#ifdef DD_EXPERIMENT_TIMING
-      if (threadIdx.x == 64) tacc2[6] += clock64() - t_entry;  // Q copied
-#endif
     }
     const bool active = x == 0 || has_b;
     const float scale_log2 = a.scale_log2;
@@ -382,14 +351,8 @@ __global__ void __launch_bounds__(TcCfg<KV>::kThreads, 1)
     float m_used = -INFINITY;
     uint64_t lsum = 0ull;  // running row sum, as two packed partial sums
     for (int j = 0; active && j < ntiles; ++j) {
-      bool ok = TCW(0, mbar_wait(&bars.s_full[x], j & 1, abort, a.err));
+      bool ok = (mbar_wait(&bars.s_full[x], j & 1, abort, a.err));
       tc_fence_after();
-      TCP_START(tp)
-#ifdef DD_EXPERIMENT_NO_SOFTMAX
-      tc_fence_before();
-      mbar_arrive(&bars.p_full[x]);
-      continue;
-#endif
       const int valid = min((j == ntiles - 1) ? (npages - kTcPagesPerTile * j - 1) * kPageSize + it.last_valid
                                               : kTcTok,
                             row_lim == INT_MAX ? kTcTok : max(row_lim - kTcTok * j, 0));
@@ -424,7 +387,6 @@ __global__ void __launch_bounds__(TcCfg<KV>::kThreads, 1)
       }
       float mt = mx * scale_log2;
       if (!ok) mt = m_used;
-      TCP_MARK(0, tp)
       // Lazy rescale: the exponentials use a stale max unless the row max
       // grew by more than 2^8. P.V_{j-1} is complete here (S_j was committed
       // after it), so O can be rescaled in place; tcgen05.ld/st are warp-wide,
@@ -439,7 +401,6 @@ __global__ void __launch_bounds__(TcCfg<KV>::kThreads, 1)
         lsum = f2_fma(lsum, f2_pack(f, f), 0ull);
         m_used = m_new;
       }
-      TCP_MARK(1, tp)
       // Pass 2: exponentials, sum, P (hi, lo) over each chunk's own scores.
       const uint64_t sc2 = f2_pack(scale_log2, scale_log2), nm2 = f2_pack(-m_used, -m_used);
 #pragma unroll
@@ -462,16 +423,11 @@ __global__ void __launch_bounds__(TcCfg<KV>::kThreads, 1)
             if (i >= vc) s[i] = -INFINITY;
         }
         softmax_chunk(s, sc2, nm2, lsum, s_col + c * 64);
-        TCP_MARK(2 + c, tp)
       }
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&bars.p_full[x]);
-      TCP_MARK(4, tp)
     }
-#ifdef DD_EXPERIMENT_TIMING
-    if (threadIdx.x == 64) tacc2[7] += clock64() - t_entry;  // all tiles done
-#endif
     // Epilogue: the normalised O row and its LSE.
     if (active) {
       const float L = f2_lo(lsum) + f2_hi(lsum);
@@ -506,15 +462,6 @@ __global__ void __launch_bounds__(TcCfg<KV>::kThreads, 1)
       if (live) a.part_lse[slot] = L > 0.f ? m_used + log2f(L) : -INFINITY;
     }
   }
-#ifdef DD_EXPERIMENT_TIMING
-  if (lane == 0)
-    for (int k = 0; k < 8; ++k) {
-      if (tacc[k])
-        atomicAdd(reinterpret_cast<unsigned long long*>(&a.err->pad[1]) + 8 + k, (unsigned long long)tacc[k]);
-      if (tacc2[k])
-        atomicAdd(reinterpret_cast<unsigned long long*>(&a.err->pad[1]) + 16 + k, (unsigned long long)tacc2[k]);
-    }
-#endif
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {

@@ -105,9 +105,6 @@ __device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* m
 }
 __device__ __forceinline__ void umma2_ss(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc,
                                          uint32_t acc) {
-#ifdef DD_EXPERIMENT_NO_QK
-  return;
-#endif
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
       " tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d),
@@ -115,9 +112,6 @@ __device__ __forceinline__ void umma2_ss(uint32_t d, uint64_t a, uint64_t b, uin
 }
 __device__ __forceinline__ void umma2_ts(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t idesc,
                                          uint32_t acc) {
-#ifdef DD_EXPERIMENT_NO_PV
-  return;
-#endif
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
       " tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d),
@@ -329,11 +323,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kT2Threads, 1)
     for (int j = 0; j < ntiles; ++j) {
       bool ok = mbar_wait_cl(&bars.s_full[x], j & 1, abort, a.err);
       tc_fence_after();
-#ifdef DD_EXPERIMENT_NO_SOFTMAX
-      tc_fence_before();
-      mbar_arrive_cluster(p_full_l);
-      continue;
-#endif
       const int valid = (j == ntiles - 1) ? (npages - kTcPagesPerTile * j - 1) * kPageSize + it.last_valid
                                           : kTcTok;
       float mx = -INFINITY;

@@ -23,7 +23,7 @@ enum ItemKind : int32_t {
   kItemMma = 1,     // warp-level tensor-core tiles, <= 64 query rows per item
   kItemTc = 2,      // tcgen05 (TMEM accumulators), up to 256 query rows per item
   kItemTc2 = 3,     // tcgen05 on a CTA pair (cta_group::2), up to 512 rows per item
-  kItemTcs = 4,     // tcgen05 streaming (tokens on M), <= 64 rows, items packed in groups
+  kItemReserved = 4,  // unused (keeps the ABI's per-kernel token array at 5 entries)
   kNumItemKinds = 5
 };
 
@@ -110,10 +110,6 @@ struct dd_plan {
   // Packed host image of everything the device needs, and its layout.
   std::vector<uint8_t> image;
   size_t off_items[dd::kNumItemKinds] = {0, 0, 0, 0, 0};
-  // Groups of kItemTcs items packed into one streaming pass: {first item,
-  // items, pages, rows}.
-  std::vector<int32_t> tcs_groups;
-  size_t off_groups = 0;
   size_t off_pages = 0, off_qorder = 0, off_pindptr = 0, off_pslots = 0;
   // Set by dd_plan_upload.
   const void* device_base = nullptr;

@@ -80,25 +80,13 @@ static int kind_for(const dd_attn_config& c, const dd_plan_options& o, int64_t r
     return kItemSimple;
   const bool tc = o.use_tensor_cores && c.head_dim == 128 && dd_tc_available();
   if (tc && o.cta_pairs && rows > 256 && c.kv_dtype == DD_DTYPE_BF16) return kItemTc2;
-#ifdef DD_EXPERIMENT_TCS
-  if (tc && rows <= 64 && c.kv_dtype == DD_DTYPE_BF16) return kItemTcs;  // in 32-row tiles
-#endif
-#ifdef DD_EXPERIMENT_TC_MIN_ROWS
-  if (tc && rows >= DD_EXPERIMENT_TC_MIN_ROWS) return kItemTc;
-#else
   if (tc && rows >= 128) return kItemTc;
-#endif
   return kItemMma;
 }
 
 static int row_tile_for(int kind) {
-  return kind == kItemTc2 ? 512 : kind == kItemTc ? 256 : kind == kItemMma ? 16 : kind == kItemTcs ? 32 : 64;
+  return kind == kItemTc2 ? 512 : kind == kItemTc ? 256 : kind == kItemMma ? 16 : 64;
 }
-
-// Packing of kItemTcs items into streaming groups.
-constexpr int kTcsMaxRows = 32;     // query rows of a group (the N of its products)
-constexpr int kTcsMaxPages = 128;   // pages of a group (16 tiles of 128 tokens)
-constexpr int kTcsChunkPages = 64;  // split of long narrow nodes
 
 // SMs of the target GPU (B200); only a load-balancing heuristic, so the
 // planner needs no device.
@@ -344,9 +332,7 @@ static void build_items(dd_plan* p) {
     const double part_bytes = (double)n.num_q * Hq * (D + 1) * 4.0 * 2.0;
     int64_t kmax = std::max<int64_t>(1, (int64_t)(kv_bytes / (8.0 * part_bytes)));
     int64_t chunk_pages = p->opts.max_chunk_pages > 0 ? p->opts.max_chunk_pages
-                          : kind == kItemTcs ? kTcsChunkPages
                           : (row_tiles == 1 ? 16 : (int64_t)1 << 30);
-    if (kind == kItemTcs) kmax = std::max<int64_t>(kmax, (n.page_count + kTcsChunkPages - 1) / kTcsChunkPages);
     int64_t k = std::min<int64_t>(kmax, (n.page_count + chunk_pages - 1) / chunk_pages);
     if ((kind == kItemTc || kind == kItemTc2) && p->opts.max_chunk_pages <= 0) {
       // Wide nodes are compute-bound: split their pages so the tensor-core
@@ -449,38 +435,6 @@ static void build_items(dd_plan* p) {
     p->live_pages += n.page_count;
     for (int32_t q = n.q_begin; q < n.q_begin + n.num_q; ++q) p->q_leaf[q] = (int32_t)ni;
   }
-  // Groups of streaming items: per KV head, consecutive items (longest
-  // first) while the group stays within kTcsMaxRows rows and kTcsMaxPages
-  // pages; the items are reordered so each group's items are contiguous.
-  p->tcs_groups.clear();
-  std::vector<WorkItem>& ti = p->items[kItemTcs];
-  if (!ti.empty()) {
-    std::vector<WorkItem> ordered;
-    ordered.reserve(ti.size());
-    std::vector<std::vector<int32_t>> by_head(Hkv);
-    for (size_t i = 0; i < ti.size(); ++i) by_head[ti[i].kv_head].push_back((int32_t)i);
-    std::vector<std::array<int32_t, 4>> groups;
-    for (int h = 0; h < Hkv; ++h) {
-      int32_t first = (int32_t)ordered.size(), n_items = 0, pages = 0, rows = 0;
-      for (int32_t i : by_head[h]) {
-        const WorkItem& it = ti[i];
-        if (n_items > 0 && (rows + it.nrows > kTcsMaxRows || pages + it.npages > kTcsMaxPages)) {
-          groups.push_back({first, n_items, pages, rows});
-          first = (int32_t)ordered.size();
-          n_items = pages = rows = 0;
-        }
-        ordered.push_back(it);
-        ++n_items;
-        pages += it.npages;
-        rows += it.nrows;
-      }
-      if (n_items > 0) groups.push_back({first, n_items, pages, rows});
-    }
-    std::stable_sort(groups.begin(), groups.end(),
-                     [](const std::array<int32_t, 4>& a, const std::array<int32_t, 4>& b) { return a[2] > b[2]; });
-    ti.swap(ordered);
-    for (const auto& g4 : groups) p->tcs_groups.insert(p->tcs_groups.end(), g4.begin(), g4.end());
-  }
 }
 
 static void pack_image(dd_plan* p) {
@@ -496,7 +450,6 @@ static void pack_image(dd_plan* p) {
   p->off_qorder = take(p->query_order.size() * sizeof(int32_t));
   p->off_pindptr = take(p->path_indptr.size() * sizeof(int32_t));
   p->off_pslots = take(p->path_slots.size() * sizeof(int32_t));
-  p->off_groups = take(p->tcs_groups.size() * sizeof(int32_t));
   p->off_qlimit = take(p->qlimit.size() * sizeof(int32_t));
   // Reused across rebuilds; alignment gaps are never read.
   p->image.resize(std::max<size_t>(off, kAlign));
@@ -509,7 +462,6 @@ static void pack_image(dd_plan* p) {
   put(p->off_qorder, p->query_order.data(), p->query_order.size() * 4);
   put(p->off_pindptr, p->path_indptr.data(), p->path_indptr.size() * 4);
   put(p->off_pslots, p->path_slots.data(), p->path_slots.size() * 4);
-  put(p->off_groups, p->tcs_groups.data(), p->tcs_groups.size() * 4);
   put(p->off_qlimit, p->qlimit.data(), p->qlimit.size() * 4);
 }
 
@@ -737,8 +689,6 @@ int dd_plan_advance(dd_plan* p, const int32_t* tokens_added, const uint32_t* new
     const int32_t leaf = p->q_leaf[pos[b]];
     if (leaf < 0 || p->nodes[leaf].num_q != 1)
       return fail(DD_ERR_NOT_AVAILABLE, "query " + std::to_string(b) + " shares its last pages; re-plan");
-    if (p->nodes[leaf].kind == kItemTcs)  // grouped items are reordered after the build
-      return fail(DD_ERR_NOT_AVAILABLE, "streaming-group items are not advanced; re-plan");
     if (p->nodes[leaf].last_valid == kPageSize) {
       if (!new_block) return fail(DD_ERR_INVALID_ARGUMENT, "new_block is NULL");
       if (new_block[b] >= (uint32_t)p->cfg.num_pages)
@@ -788,6 +738,10 @@ int dd_plan_advance(dd_plan* p, const int32_t* tokens_added, const uint32_t* new
     }
   }
   pack_image(p);
+  // The image's layout changed: a decode before the next dd_plan_upload must
+  // fail instead of reading the old image at the new offsets.
+  p->device_base = nullptr;
+  p->device_id = -1;
   return DD_OK;
 }
 

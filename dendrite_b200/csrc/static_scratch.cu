@@ -22,7 +22,9 @@ static __device__ __align__(256) uint8_t g_static_scratch[kStaticScratchBytes];
 
 // Device address of g_static_scratch on the current device, looked up once per
 // device. In host code the symbol's name is only a host-side stand-in, so the
-// kernels are always given this address.
+// kernels are always given this address. The cached address outlives no
+// device reset: after cudaDeviceReset the module is loaded again and the
+// array may move (documented in the header).
 static int static_scratch_ptr(void** out) {
   static std::mutex mu;
   static void* addr[kMaxDevices] = {};
@@ -70,4 +72,12 @@ extern "C" int dd_decode_paged_static(const dd_attn_config* cfg, int32_t batch_s
   // needed between calls.
   return dd_decode_paged(cfg, batch_size, max_pages_per_seq, q, kv_pages, kv_scales, page_indptr,
                          page_indices, num_tokens, out, lse, scratch, kStaticScratchBytes, stream);
+}
+
+extern "C" int dd_decode_paged_static_status(dd_stream_t stream, uint32_t* code, uint32_t* aux) {
+  if (!code) return fail(DD_ERR_INVALID_ARGUMENT, "code is NULL");
+  void* scratch = nullptr;
+  const int rc = static_scratch_ptr(&scratch);
+  if (rc) return rc;
+  return dd_workspace_status(scratch, stream, code, aux);
 }

@@ -185,7 +185,9 @@ int dd_plan_rebuild(dd_plan* plan, int32_t batch_size, const int32_t* block_indp
  * place only for queries that own their last pages (a leaf of the plan's
  * tree with no other query): their nodes gain the token / block and their
  * items are re-cut; the device image must be uploaded again (its size,
- * dd_plan_get_info().device_bytes, can grow by the moved page runs). Returns
+ * dd_plan_get_info().device_bytes, can grow by the moved page runs): a
+ * successful advance forgets the previous upload, so dd_cascade_decode
+ * returns DD_ERR_INVALID_ARGUMENT until the plan is uploaded again. Returns
  * DD_ERR_NOT_AVAILABLE, with the plan unchanged, when some query shares its
  * last pages (a fresh fork, a copy-on-write pending), for prefill and flat
  * plans, or when the page list needs compacting: the caller then re-plans
@@ -273,12 +275,22 @@ int dd_profile_read(double* ms, int64_t* launches, int32_t n);
  * call before any stream capture. Every call shares the one array, so calls
  * whose executions overlap on the GPU (different streams, or different host
  * threads on one device) race and corrupt each other's results: serialise
- * them. The function calls no cudaMalloc / cudaFree. */
+ * them. The device address is looked up once per device and kept for the
+ * life of the process: do not use this entry point on a device after
+ * cudaDeviceReset (or any other destruction of its primary context) in the
+ * same process. The function calls no cudaMalloc / cudaFree. */
 int dd_decode_paged_static(const dd_attn_config* cfg, int32_t batch_size,
                            int32_t max_pages_per_seq, const void* q, const void* kv_pages,
                            const void* kv_scales, const int32_t* page_indptr,
                            const int32_t* page_indices, const int32_t* num_tokens, void* out,
                            float* lse, dd_stream_t stream);
+/* Device status of the last dd_decode_paged_static call on the current
+ * device, as dd_workspace_status reports it for a caller workspace (0 = OK;
+ * otherwise an error code such as a bounded-wait timeout or an out-of-range
+ * page id, with its detail in *aux). Reads the status words at the head of
+ * the static scratch on `stream` and synchronises it. No counterpart in the
+ * reference. */
+int dd_decode_paged_static_status(dd_stream_t stream, uint32_t* code, uint32_t* aux);
 
 /* Merge of attention states: (o_a, lse_a) (+) (o_b, lse_b) -> (o, lse), f32,
  * natural-log LSE, element-wise over n rows of head_dim. The batched form of

@@ -44,6 +44,9 @@ def _load():
         "or_prefill": (None, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_float, vp, vp, vp, vp]),
         "or_decode_batch": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_float, vp,
                                       C.c_int, i64, vp, vp, vp, vp, vp, vp, C.c_int]),
+        "or_decode_batch_ws": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_float, vp,
+                                         C.c_int, i64, vp, vp, vp, vp, vp, vp, C.c_int, vp, C.c_size_t]),
+        "or_decode_scratch_floats": (C.c_size_t, [C.c_int, C.c_int, C.c_int, C.c_int]),
         "or_merge_states": (None, [C.c_int, C.c_int, vp, vp, vp, vp, vp, vp]),
         "or_quant_per_head": (None, [vp, C.c_int, i64, C.c_int, C.c_int, C.c_int, vp, vp]),
         "or_quant_mx": (None, [vp, C.c_int, i64, vp, vp]),
@@ -145,10 +148,22 @@ def prefill(q: np.ndarray, k: np.ndarray, v: np.ndarray, scale: float = 0.0) -> 
     return out
 
 
+class DecodeScratch:
+    """Per-thread gather / repeat scratch of decode_batch, allocated and
+    touched once so repeated (timed) calls do not pay for page faults."""
+
+    def __init__(self, threads: int, Hq: int, Hkv: int, D: int, max_tokens: int):
+        self.threads = int(threads)
+        self.per_thread = int(lib.or_decode_scratch_floats(Hq, Hkv, D, int(max_tokens)))
+        self.buf = np.ones(self.threads * self.per_thread, dtype=np.float32)
+
+
 def decode_batch(q: np.ndarray, pool: np.ndarray, indptr, block_ids, num_tokens, num_kv_heads: int,
-                 gqa_grouped: bool = False, scale: float = 0.0, threads: int | None = None):
+                 gqa_grouped: bool = False, scale: float = 0.0, threads: int | None = None,
+                 scratch: DecodeScratch | None = None):
     """ReferenceBackend::decode_batch. q [B][Hq][D] f32; pool f32 or bf16 bits.
-    Returns (out f32 [B][Hq][D], lse f32 [B][Hq] natural log)."""
+    Returns (out f32 [B][Hq][D], lse f32 [B][Hq] natural log). With scratch,
+    its threads run the batch in its preallocated buffers."""
     q = np.ascontiguousarray(q, dtype=np.float32)
     pool, dt = _pool_arg(np.ascontiguousarray(pool))
     B, Hq, D = q.shape
@@ -159,6 +174,11 @@ def decode_batch(q: np.ndarray, pool: np.ndarray, indptr, block_ids, num_tokens,
     ntok = np.ascontiguousarray(num_tokens, dtype=np.int32)
     out = np.empty((B, Hq, D), dtype=np.float32)
     lse = np.empty((B, Hq), dtype=np.float32)
+    if scratch is not None:
+        lib.or_decode_batch_ws(B, Hq, num_kv_heads, D, 1 if gqa_grouped else 0, scale, _p(pool), dt,
+                               pool.shape[0], _p(q), _p(indptr), _p(ids), _p(ntok), _p(out),
+                               _p(lse), scratch.threads, _p(scratch.buf), scratch.per_thread)
+        return out, lse
     threads = threads or os.cpu_count() or 1
     lib.or_decode_batch(B, Hq, num_kv_heads, D, 1 if gqa_grouped else 0, scale, _p(pool), dt,
                         pool.shape[0], _p(q), _p(indptr), _p(ids), _p(ntok), _p(out), _p(lse),

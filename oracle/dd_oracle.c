@@ -181,6 +181,9 @@ typedef struct {
   int B;
   int next;         /* work counter */
   pthread_mutex_t mu;
+  float* ws;        /* caller scratch: ws_per_thread floats per worker, or NULL */
+  size_t ws_per_thread;
+  int next_ws;      /* next worker's scratch slice */
 } decode_job;
 
 /* One query, literally as ReferenceBackend::decode: gather -> cat -> repeat ->
@@ -269,16 +272,33 @@ static int max_tokens(const decode_job* j) {
   return m;
 }
 
+/* Scratch floats one worker needs for queries of up to T tokens. */
+size_t or_decode_scratch_floats(int Hq, int Hkv, int D, int T) {
+  const size_t kvsz = (size_t)Hkv * T * D, repsz = (size_t)Hq * T * D;
+  return 2 * (kvsz ? kvsz : 1) + 2 * (repsz ? repsz : 1) + (T ? T : 1);
+}
+
 static void* decode_worker(void* arg) {
   decode_job* j = (decode_job*)arg;
   const int T = max_tokens(j);
   const size_t kvsz = (size_t)j->Hkv * T * j->D, repsz = (size_t)j->Hq * T * j->D;
-  float* sk = (float*)malloc(sizeof(float) * (kvsz ? kvsz : 1));
-  float* sv = (float*)malloc(sizeof(float) * (kvsz ? kvsz : 1));
-  float* rk = (float*)malloc(sizeof(float) * (repsz ? repsz : 1));
-  float* rv = (float*)malloc(sizeof(float) * (repsz ? repsz : 1));
-  float* sc = (float*)malloc(sizeof(float) * (T ? T : 1));
-  if (sk && sv && rk && rv && sc) {
+  const size_t need = or_decode_scratch_floats(j->Hq, j->Hkv, j->D, T);
+  float* base = NULL;
+  int owned = 0;
+  if (j->ws && j->ws_per_thread >= need) {
+    pthread_mutex_lock(&j->mu);
+    base = j->ws + (size_t)j->next_ws++ * j->ws_per_thread;
+    pthread_mutex_unlock(&j->mu);
+  } else {
+    base = (float*)malloc(sizeof(float) * need);
+    owned = 1;
+  }
+  if (base) {
+    float* sk = base;
+    float* sv = sk + (kvsz ? kvsz : 1);
+    float* rk = sv + (kvsz ? kvsz : 1);
+    float* rv = rk + (repsz ? repsz : 1);
+    float* sc = rv + (repsz ? repsz : 1);
     for (;;) {
       pthread_mutex_lock(&j->mu);
       const int b = j->next++;
@@ -287,22 +307,26 @@ static void* decode_worker(void* arg) {
       decode_one(j, b, sk, sv, rk, rv, sc);
     }
   }
-  free(sk); free(sv); free(rk); free(rv); free(sc);
+  if (owned) free(base);
   return NULL;
 }
 
 /* ReferenceBackend::decode_batch over B queries with `threads` workers.
+ * ws, when not NULL, holds ws_per_thread floats for each worker (at least
+ * or_decode_scratch_floats of the batch's longest table), so a timed loop can
+ * keep the gather / repeat scratch allocated and touched across calls.
  * Returns 0 on success. */
-int or_decode_batch(int B, int Hq, int Hkv, int D, int gqa_grouped, float scale,
-                    const void* pool, int pool_dtype, int64_t num_pages, const float* q,
-                    const int32_t* indptr, const uint32_t* ids, const int32_t* ntok, float* out,
-                    float* lse, int threads) {
+int or_decode_batch_ws(int B, int Hq, int Hkv, int D, int gqa_grouped, float scale,
+                       const void* pool, int pool_dtype, int64_t num_pages, const float* q,
+                       const int32_t* indptr, const uint32_t* ids, const int32_t* ntok, float* out,
+                       float* lse, int threads, float* ws, size_t ws_per_thread) {
   decode_job j;
   j.Hq = Hq; j.Hkv = Hkv; j.D = D; j.gqa_grouped = gqa_grouped;
   j.scale = scale > 0.0f ? scale : 1.0f / sqrtf((float)D);
   j.pool = pool; j.pool_dtype = pool_dtype; j.num_pages = num_pages;
   j.q = q; j.indptr = indptr; j.ids = ids; j.ntok = ntok; j.out = out; j.lse = lse;
   j.B = B; j.next = 0;
+  j.ws = ws; j.ws_per_thread = ws_per_thread; j.next_ws = 0;
   pthread_mutex_init(&j.mu, NULL);
   if (threads < 1) threads = 1;
   if (threads > 1024) threads = 1024;
@@ -315,6 +339,15 @@ int or_decode_batch(int B, int Hq, int Hkv, int D, int gqa_grouped, float scale,
   free(tid);
   pthread_mutex_destroy(&j.mu);
   return 0;
+}
+
+/* The same with per-worker scratch allocated (and first touched) inside. */
+int or_decode_batch(int B, int Hq, int Hkv, int D, int gqa_grouped, float scale,
+                    const void* pool, int pool_dtype, int64_t num_pages, const float* q,
+                    const int32_t* indptr, const uint32_t* ids, const int32_t* ntok, float* out,
+                    float* lse, int threads) {
+  return or_decode_batch_ws(B, Hq, Hkv, D, gqa_grouped, scale, pool, pool_dtype, num_pages, q,
+                            indptr, ids, ntok, out, lse, threads, NULL, 0);
 }
 
 /* ReferenceBackend::prefill (crates/dendrite-core/src/attention/backend.rs:

@@ -25,3 +25,24 @@ def test_reference_arm_line(workload, unit):
     e2e = line["e2e"]
     assert e2e["value"] == line["value"] and e2e["unit"] == unit
     assert e2e["h2d_bytes_per_step"] == 0 and e2e["d2h_bytes_per_step"] == 0
+
+
+def test_reference_arm_maps_no_product_library():
+    """The reference arm times only the CPU restatement: the process must not
+    load libdendrite_b200.so (not even by importing the package)."""
+    code = (
+        "import runpy, sys\n"
+        "sys.argv = ['bench.py', '--impl', 'reference', '--workload', 'quant-mxfp8', '--steps', '1', "
+        "'--warmup', '0']\n"
+        "runpy.run_path('bench.py', run_name='__main__')\n"
+        "maps = open('/proc/self/maps').read()\n"
+        "print('PRODUCT_SO_LOADED' if 'libdendrite_b200' in maps else 'PRODUCT_SO_ABSENT')\n")
+    out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=600,
+                         cwd=ROOT)
+    assert out.returncode == 0, out.stderr[-2000:]
+    assert "PRODUCT_SO_ABSENT" in out.stdout
+    code2 = code.replace("'quant-mxfp8'", "'mcts8b'")
+    out = subprocess.run([sys.executable, "-c", code2], capture_output=True, text=True, timeout=600,
+                         cwd=ROOT)
+    assert out.returncode == 0, out.stderr[-2000:]
+    assert "PRODUCT_SO_ABSENT" in out.stdout

@@ -36,3 +36,23 @@ def test_decode_after_advance(cuda):
     ref, _ = oracle.decode_batch(bits_to_f32(q), pool, indptr, np.concatenate(tables).astype(np.uint32),
                                  ntok, 8)
     assert_close(out.float().cpu().numpy(), bits_to_f32(bf16_bits(ref)), what="after advance")
+
+
+def test_advance_forgets_the_upload(cuda):
+    """An advance repacks the plan image (new offsets, possibly larger), so a
+    decode before the next upload must be refused, not read the old image."""
+    tb = wl.small_tree(9, Hq=8, Hkv=2, D=128, prefix=64, levels=((2, 16, 48),),
+                       leaves_per_node=2, suffix=(1, 40))
+    P = tb.num_pages + 2 * tb.batch_size
+    cfg = dd.make_config(8, 2, 128, P)
+    tables, ntok = tb.tables(), tb.num_tokens.copy()
+    plan = dd.CascadePlan(cfg, tb.indptr, tb.block_ids, ntok)
+    plan.upload(cuda)
+    assert plan.advance(*_grow(tables, ntok, iter(range(tb.num_pages, P))))
+    q = torch.zeros(tb.batch_size, 8, 128, dtype=torch.bfloat16, device=cuda)
+    pool = torch.zeros(P, 2, 2, 16, 128, dtype=torch.bfloat16, device=cuda)
+    with pytest.raises(dd.InvalidArgument, match="not uploaded"):
+        dd.cascade_decode(cfg, plan, q, pool)
+    plan.upload(cuda)
+    dd.cascade_decode(cfg, plan, q, pool)
+    torch.cuda.synchronize()
