@@ -430,6 +430,27 @@ def e2e_time(e2e_step, args, world, dev):
     return float(t.item())
 
 
+def pool_pages(tb) -> int:
+    """Pages of the timed pool: the tree's, plus spare pages for the
+    end-to-end loop, whose leaves grow a token a step."""
+    return tb.num_pages + tb.batch_size * (E2E_MAX_STEPS // 16 + 2)
+
+
+def device_inputs(tb, num_pages: int, seed: int, dev):
+    """Seeded N(0,1) bf16 page pool [num_pages][2][Hkv][16][D] and queries
+    [B][Hq][D] on the device (the parity tests of the timed configs rebuild
+    them with this function)."""
+    import torch
+
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(seed)
+    pool = torch.randn((num_pages, 2, tb.num_kv_heads, 16, tb.head_dim), generator=gen, device=dev,
+                       dtype=torch.float32).to(torch.bfloat16)
+    q = torch.randn((tb.batch_size, tb.num_qo_heads, tb.head_dim), generator=gen, device=dev,
+                    dtype=torch.float32).to(torch.bfloat16)
+    return pool, q
+
+
 def run_tree(args, world, rank, local, dev):
     import torch
     import torch.distributed as dist
@@ -446,14 +467,8 @@ def run_tree(args, world, rank, local, dev):
 
     tb, total_queries = make_tree(args.workload, rank, world)
     Hq, Hkv, D, B = tb.num_qo_heads, tb.num_kv_heads, tb.head_dim, tb.batch_size
-    gen = torch.Generator(device=dev)
-    gen.manual_seed(SEED if heads else SEED + rank)
-    # Spare pages for the end-to-end loop, whose leaves grow a token a step.
-    spare = B * (E2E_MAX_STEPS // 16 + 2)
-    num_pages = tb.num_pages + spare
-    pool = torch.randn((num_pages, 2, Hkv, 16, D), generator=gen, device=dev,
-                       dtype=torch.float32).to(torch.bfloat16)
-    q = torch.randn((B, Hq, D), generator=gen, device=dev, dtype=torch.float32).to(torch.bfloat16)
+    num_pages = pool_pages(tb)
+    pool, q = device_inputs(tb, num_pages, SEED if heads else SEED + rank, dev)
     scales = None
     kv_dtype, elem, scale_bytes = _lib.DTYPE_BF16, 2.0, 0.0
     if kv != "bf16":
