@@ -493,7 +493,7 @@ def run_tree(args, world, rank, local, dev):
     def make_plan():
         if pb is not None:
             return dd.CascadePlan.prefill(lcfg, pb.indptr, pb.block_ids, pb.prefix_len, pb.num_new)
-        return dd.CascadePlan(lcfg, tb.indptr, tb.block_ids, tb.num_tokens)
+        return dd.CascadePlan(lcfg, tb.indptr, tb.block_ids, tb.num_tokens, tc_sms=args.tc_sms)
 
     plan = make_plan()
     plan.upload(dev)
@@ -630,7 +630,7 @@ def run_tree(args, world, rank, local, dev):
             "config": {"workload": args.workload, "desc": w["desc"], "heads": [Hq, Hkv, D],
                        "queries": total_queries, "pages_per_rank": tb.num_pages,
                        "unique_kv_tokens_per_rank": info.kv_tokens,
-                       "flat_kv_tokens_per_rank": info.kv_tokens_flat, "plan_nodes": info.num_nodes,
+                       "flat_kv_tokens_per_rank": info.kv_tokens_flat, "plan_nodes": info.num_nodes, "tc_ctas": info.tc_ctas,
                        "l2": "flushed between steps (256 MiB write, untimed)",
                        "parallelism": f"{w['split']} x{world}"},
             "effective_gbs": gbs, "hbm_frac": gbs / (hbm_peak * world),
@@ -743,6 +743,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="mcts8b")
     ap.add_argument("--cpu-budget", type=float, default=10.0)
+    ap.add_argument("--tc-sms", type=int, default=0,
+                    help="SMs of the tcgen05 kernel while the streaming kernel runs (plan option "
+                         "tc_sms: 0 = cost model, -1 = one CTA per item)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--clocks-csv", default=None,
                     help="also write the raw nvidia-smi clock samples of the timed region here")

@@ -66,7 +66,7 @@ class AttnConfig(C.Structure):
 
 class PlanOptions(C.Structure):
     _fields_ = [("share_prefixes", C.c_int32), ("max_chunk_pages", C.c_int32),
-                ("use_tensor_cores", C.c_int32), ("cta_pairs", C.c_int32)]
+                ("use_tensor_cores", C.c_int32), ("cta_pairs", C.c_int32), ("tc_sms", C.c_int32)]
 
 
 class PlanInfo(C.Structure):
@@ -74,7 +74,7 @@ class PlanInfo(C.Structure):
                 ("max_depth", C.c_int32), ("kv_tokens", C.c_int64),
                 ("kv_tokens_flat", C.c_int64), ("workspace_bytes", C.c_size_t),
                 ("device_bytes", C.c_size_t), ("kv_tokens_by_kernel", C.c_int64 * 5),
-                ("tc_row_tokens", C.c_int64)]
+                ("tc_row_tokens", C.c_int64), ("tc_ctas", C.c_int32)]
 
 
 class QuantConfig(C.Structure):

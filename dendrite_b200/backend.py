@@ -122,14 +122,15 @@ class CascadePlan:
     (the batch builder's output; see dd_plan_create)."""
 
     def __init__(self, cfg: AttnConfig, indptr, block_ids, num_tokens, share_prefixes: bool = True,
-                 max_chunk_pages: int = 0, use_tensor_cores: bool = True, cta_pairs: bool = False):
+                 max_chunk_pages: int = 0, use_tensor_cores: bool = True, cta_pairs: bool = False,
+                 tc_sms: int = 0):
         self.cfg = cfg
         self._indptr = np.ascontiguousarray(indptr, dtype=np.int32)
         self._ids = np.ascontiguousarray(block_ids, dtype=np.uint32)
         self._ntok = np.ascontiguousarray(num_tokens, dtype=np.int32)
         self.batch_size = len(self._ntok)
         opts = PlanOptions(1 if share_prefixes else 0, max_chunk_pages, 1 if use_tensor_cores else 0,
-                           1 if cta_pairs else 0)
+                           1 if cta_pairs else 0, tc_sms)
         h = C.c_void_p()
         rc = lib.dd_plan_create(C.byref(cfg), self.batch_size,
                                 self._indptr.ctypes.data_as(_lib._I32P),
@@ -153,7 +154,7 @@ class CascadePlan:
         self._new = np.ascontiguousarray(num_new, dtype=np.int32)
         self._ntok = self._prefix + self._new
         self.batch_size = int(self._new.sum())
-        opts = PlanOptions(1, 0, 1 if use_tensor_cores else 0, 0)
+        opts = PlanOptions(1, 0, 1 if use_tensor_cores else 0, 0, 0)
         h = C.c_void_p()
         rc = lib.dd_plan_create_prefill(C.byref(cfg), len(self._new),
                                         self._indptr.ctypes.data_as(_lib._I32P),

@@ -12,9 +12,9 @@
 
 namespace dd {
 cudaError_t launch_attn_simple(const AttnArgs& a, dim3 grid, cudaStream_t st);
-int launch_attn_mma(const AttnArgs& a, int64_t num_pages, cudaStream_t st);
+int launch_attn_mma(const AttnArgs& a, int64_t num_pages, cudaStream_t st, bool after_tc);
 bool mma_supported(int D, int kv_dtype);
-int launch_attn_tc(const AttnArgs& a, int64_t num_pages, int num_items, cudaStream_t st);
+int launch_attn_tc(const AttnArgs& a, int64_t num_pages, int grid, cudaStream_t st);
 int launch_attn_tc2(const AttnArgs& a, int64_t num_pages, int num_items, cudaStream_t st);
 cudaError_t launch_merge(const MergeArgs& a, cudaStream_t st);
 
@@ -90,30 +90,6 @@ extern "C" int dd_plan_upload(dd_plan* p, void* buf, size_t bytes, dd_stream_t s
   return DD_OK;
 }
 
-// One side stream and fork/join events per host thread and device: calls
-// from different threads never share events.
-struct SideStream {
-  cudaStream_t stream = nullptr;
-  cudaEvent_t fork = nullptr, join = nullptr;
-};
-
-static SideStream* side_stream() {
-  constexpr int kMaxDevices = 64;
-  thread_local SideStream per_dev[kMaxDevices];
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
-  SideStream& s = per_dev[dev];
-  if (!s.stream) {
-    if (cudaStreamCreateWithFlags(&s.stream, cudaStreamNonBlocking) != cudaSuccess ||
-        cudaEventCreateWithFlags(&s.fork, cudaEventDisableTiming) != cudaSuccess ||
-        cudaEventCreateWithFlags(&s.join, cudaEventDisableTiming) != cudaSuccess) {
-      s = SideStream{};
-      return nullptr;
-    }
-  }
-  return &s;
-}
-
 extern "C" int dd_cascade_decode(const dd_attn_config* cfg, const dd_plan* p, const void* q,
                                  const void* kv, const void* scales, void* out, float* lse,
                                  void* ws, size_t ws_bytes, dd_stream_t stream) {
@@ -137,30 +113,31 @@ extern "C" int dd_cascade_decode(const dd_attn_config* cfg, const dd_plan* p, co
   a.pages = reinterpret_cast<const uint32_t*>(base + p->off_pages);
   a.qorder = reinterpret_cast<const int32_t*>(base + p->off_qorder);
   a.qlimit = p->causal ? reinterpret_cast<const int32_t*>(base + p->off_qlimit) : nullptr;
-  // The tensor-core kernel (wide shared nodes, compute-bound) runs on a side
-  // stream forked from `st`, concurrently with the streaming kernel (narrow
-  // nodes, HBM-bound); the merge waits for both. The fork/join is a pair of
-  // events, so it also captures into a CUDA graph.
+  // The tcgen05 kernel (wide shared nodes, compute-bound) runs on tc_ctas
+  // SMs and the streaming kernel (narrow nodes, HBM-bound), launched after it
+  // in the same stream as a programmatic dependent, starts at once on the
+  // other SMs and takes each tcgen05 CTA's SM when that CTA finishes; it
+  // completes only after the tcgen05 grid, so the merge sees both. While
+  // per-launch timing is on (dd_profile_enable), launches run one after the
+  // other so each event pair brackets one kernel.
   const int n_tc = (int)p->items[kItemTc].size();
   const int n_tc2 = (int)p->items[kItemTc2].size();
-  const bool fork = n_tc + n_tc2 > 0 && !prof_timing_on() &&
-                    (!p->items[kItemMma].empty() || !p->items[kItemSimple].empty());
-  SideStream* side = nullptr;
-  if (fork) {
-    side = side_stream();
-    if (!side) return fail(DD_ERR_CUDA, "side stream creation failed");
-    e = cudaEventRecord(side->fork, st);
-    if (e == cudaSuccess) e = cudaStreamWaitEvent(side->stream, side->fork, 0);
-    if (e != cudaSuccess) return cuda_fail(e, "side stream fork");
-  }
   if (n_tc2) {
     a.items = reinterpret_cast<const WorkItem*>(base + p->off_items[kItemTc2]);
-    rc = launch_attn_tc2(a, cfg->num_pages, n_tc2, fork ? side->stream : st);
+    rc = launch_attn_tc2(a, cfg->num_pages, n_tc2, st);
     if (rc) return rc;
   }
   if (n_tc) {
     a.items = reinterpret_cast<const WorkItem*>(base + p->off_items[kItemTc]);
-    rc = launch_attn_tc(a, cfg->num_pages, n_tc, fork ? side->stream : st);
+    int grid = n_tc;
+    if (p->tc_ctas > 0) {
+      // A fixed number of CTAs, each running its scheduled items in turn.
+      a.tc_order = reinterpret_cast<const int32_t*>(base + p->off_tc_order);
+      a.tc_cta_begin = reinterpret_cast<const int32_t*>(base + p->off_tc_cta_begin);
+      grid = p->tc_ctas;
+    }
+    rc = launch_attn_tc(a, cfg->num_pages, grid, st);
+    a.tc_order = a.tc_cta_begin = nullptr;
     if (rc) return rc;
   }
   for (int k = 0; k < kNumItemKinds; ++k) {
@@ -172,14 +149,9 @@ extern "C" int dd_cascade_decode(const dd_attn_config* cfg, const dd_plan* p, co
       if (e != cudaSuccess) return cuda_fail(e, "attn_simple launch");
     } else {
       a.num_items = n;
-      rc = launch_attn_mma(a, cfg->num_pages, st);
+      rc = launch_attn_mma(a, cfg->num_pages, st, n_tc > 0 && !prof_timing_on());
       if (rc) return rc;
     }
-  }
-  if (fork) {
-    e = cudaEventRecord(side->join, side->stream);
-    if (e == cudaSuccess) e = cudaStreamWaitEvent(st, side->join, 0);
-    if (e != cudaSuccess) return cuda_fail(e, "side stream join");
   }
   MergeArgs m;
   m.part_o = a.part_o;
@@ -240,7 +212,7 @@ extern "C" int dd_decode_paged(const dd_attn_config* cfg, int32_t B, int32_t max
   const dim3 grid(ns, cfg->num_kv_heads * a.row_tiles, B);
   if (mma) {
     a.num_items = ns * cfg->num_kv_heads * a.row_tiles * B;
-    rc = launch_attn_mma(a, cfg->num_pages, st);
+    rc = launch_attn_mma(a, cfg->num_pages, st, false);
     if (rc) return rc;
   } else {
     e = launch_attn_simple(a, grid, st);

@@ -44,7 +44,15 @@
 namespace dd {
 
 constexpr int kMmaRows = 16;       // query rows per work item
-constexpr int kStreams = 4;        // independent streams per CTA
+#ifndef DD_MMA_BF16_PAIR
+#define DD_MMA_BF16_PAIR 0
+#endif
+#ifndef DD_MMA_BF16_STREAMS
+#define DD_MMA_BF16_STREAMS 4
+#endif
+#ifndef DD_MMA_BF16_STAGES
+#define DD_MMA_BF16_STAGES 3
+#endif
 constexpr int kStepPages = 2;      // pages per stage
 constexpr int kItemSlots = 2;      // item descriptors per stream
 
@@ -57,7 +65,9 @@ struct MmaCfg {
   static constexpr int kMxBytes = KV == kKvMx ? kPageSize * (D / 32) : 0;
   // Stages are read in place by the consumer; FP8 stages are a quarter (E4M3)
   // of the bf16 ones, so the FP8 rings are deeper for the same bytes in flight.
-  static constexpr int kStages = KV == kKvBf16 ? 3 : 5;
+  static constexpr bool kPair = KV != kKvBf16 || (D == 128 && DD_MMA_BF16_PAIR);
+  static constexpr int kStreams = KV == kKvBf16 ? DD_MMA_BF16_STREAMS : 4;  // independent streams per CTA
+  static constexpr int kStages = KV == kKvBf16 ? DD_MMA_BF16_STAGES : 5;
   static constexpr int kRawStage = 2 * kStepPages * kSliceRaw;         // K0 K1 V0 V1
   static constexpr int kMxStage = 2 * kStepPages * kMxBytes;
   static constexpr int kStageAll = kRawStage;                          // 1 KiB multiple (swizzle)
@@ -69,10 +79,12 @@ struct MmaCfg {
   // issue-bound): consumer h takes page h of each stage, and at the end of an
   // item consumer 1 hands its softmax state to consumer 0 through kXBytes of
   // shared memory (68 floats per lane).
-  static constexpr bool kPair = KV != kKvBf16;
   static constexpr int kConsumers = kPair ? 2 * kStreams : kStreams;
   static constexpr int kThreads = (kConsumers + kStreams) * 32;  // consumers, then producers
-  static constexpr int kXBytes = kPair ? 68 * 32 * 4 : 0;
+  // Four consumer-pair streams: 384 threads, whose warpgroups (two of
+  // consumers, one of producers) move registers to the consumers.
+  static constexpr bool kSetMaxNreg = kPair && kStreams == 4;
+  static constexpr int kXBytes = kPair ? (D / 2 + 4) * 32 * 4 : 0;
   static constexpr int kSmemBytes = kStreams * (kStreamBytes + kXBytes) + 1024;   // + alignment slack
 };
 
@@ -146,6 +158,7 @@ __global__ void __launch_bounds__(MmaCfg<D, KV>::kThreads, 1)
   static_assert(KV == kKvBf16 || D == 128, "FP8 fragments are laid out for head_dim 128");
   constexpr int S = C::kStages;
   extern __shared__ uint8_t smem_raw[];
+  constexpr int kStreams = C::kStreams;
   __shared__ StreamShared ss[kStreams];
   __shared__ int abort_flag;
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
@@ -168,7 +181,7 @@ __global__ void __launch_bounds__(MmaCfg<D, KV>::kThreads, 1)
   }
   if (threadIdx.x == kCons * 32) prefetch_tmap(&kv_map);
   __syncthreads();
-  if (C::kPair) {
+  if (C::kSetMaxNreg) {
     // 384 threads launch at 168 registers (64,512); the producer warpgroup
     // gives up to 56 and the two consumer warpgroups take 224:
     // 128 x 56 + 256 x 224 = 64,512.
@@ -704,6 +717,12 @@ __global__ void __launch_bounds__(MmaCfg<D, KV>::kThreads, 1)
       }
     }
   }
+  // Launched as a programmatic dependent of the tcgen05 kernel (cascade
+  // decode), this grid starts while that one runs, on the SMs it leaves free
+  // and on each SM it gives up; it completes only after it, so the merge that
+  // follows in the stream sees both kernels' partial states. Without a
+  // prerequisite grid the wait returns at once.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   __syncthreads();
 }
 
@@ -766,23 +785,44 @@ int make_kv_tensor_map(CUtensorMap* map, const void* kv, int64_t num_pages, int 
 }
 
 template <int D, int KV>
-static cudaError_t launch_mma_t(const CUtensorMap& map, const AttnArgs& a, cudaStream_t st) {
+static cudaError_t launch_mma_t(const CUtensorMap& map, const AttnArgs& a, cudaStream_t st,
+                               bool after_tc) {
   const int smem = MmaCfg<D, KV>::kSmemBytes;
   cudaError_t e = cudaFuncSetAttribute(attn_mma_kernel<D, KV>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
+  if (MmaCfg<D, KV>::kSetMaxNreg) {
+    // setmaxnreg.inc waits until the producers' setmaxnreg.dec has freed
+    // enough registers: 128 x (R - 56) >= 256 x (224 - R) needs R >= 168 at
+    // launch, so a build that allocates fewer must not launch.
+    cudaFuncAttributes fa;
+    e = cudaFuncGetAttributes(&fa, attn_mma_kernel<D, KV>);
+    if (e != cudaSuccess) return e;
+    if (fa.numRegs < 168) return cudaErrorInvalidConfiguration;
+  }
   int dev = 0, sms = 148, per_sm = 1;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, attn_mma_kernel<D, KV>, MmaCfg<D, KV>::kThreads, smem);
   if (e != cudaSuccess) return e;
-  const int ctas_needed = (a.num_items + kStreams - 1) / kStreams;
+  const int ctas_needed = (a.num_items + MmaCfg<D, KV>::kStreams - 1) / MmaCfg<D, KV>::kStreams;
   int grid = std::max(1, std::min(ctas_needed, sms * std::max(per_sm, 1)));
-  {
-    ProfScope ps(kProfMma, st);
-    attn_mma_kernel<D, KV><<<grid, MmaCfg<D, KV>::kThreads, smem, st>>>(map, a);
+  ProfScope ps(kProfMma, st);
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = dim3(grid);
+  lc.blockDim = dim3(MmaCfg<D, KV>::kThreads);
+  lc.dynamicSmemBytes = smem;
+  lc.stream = st;
+  cudaLaunchAttribute attr[1];
+  if (after_tc) {
+    // Programmatic dependent launch: the grid may start once every CTA of
+    // the preceding tcgen05 kernel has started (it signals at its start).
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    lc.attrs = attr;
+    lc.numAttrs = 1;
   }
-  return cudaGetLastError();
+  return cudaLaunchKernelEx(&lc, attn_mma_kernel<D, KV>, map, a);
 }
 
 bool mma_supported(int D, int kv_dtype) {
@@ -795,7 +835,7 @@ int mma_row_tile() { return kMmaRows; }
 
 // Launches the persistent kernel over a.num_items work items. The work
 // counter in the workspace header must be zero (the caller resets the header).
-int launch_attn_mma(const AttnArgs& a, int64_t num_pages, cudaStream_t st) {
+int launch_attn_mma(const AttnArgs& a, int64_t num_pages, cudaStream_t st, bool after_tc) {
   if (a.num_items <= 0) return DD_OK;
   CUtensorMap map;
   const int eb = a.kv_dtype == DD_DTYPE_BF16 ? 2 : 1;
@@ -804,11 +844,11 @@ int launch_attn_mma(const AttnArgs& a, int64_t num_pages, cudaStream_t st) {
   if (rc) return rc;
   cudaError_t e;
   if (a.kv_dtype == DD_DTYPE_BF16)
-    e = a.D == 64 ? launch_mma_t<64, kKvBf16>(map, a, st) : launch_mma_t<128, kKvBf16>(map, a, st);
+    e = a.D == 64 ? launch_mma_t<64, kKvBf16>(map, a, st, after_tc) : launch_mma_t<128, kKvBf16>(map, a, st, after_tc);
   else if (a.kv_dtype == DD_DTYPE_E4M3)
-    e = launch_mma_t<128, kKvE4m3>(map, a, st);
+    e = launch_mma_t<128, kKvE4m3>(map, a, st, after_tc);
   else
-    e = launch_mma_t<128, kKvMx>(map, a, st);
+    e = launch_mma_t<128, kKvMx>(map, a, st, after_tc);
   if (e != cudaSuccess) return fail(DD_ERR_CUDA, std::string("attn_mma launch: ") + cudaGetErrorString(e));
   return DD_OK;
 }

@@ -314,6 +314,11 @@ struct AttnArgs {
   // Causal (prefill) plans: tokens of its node (from the node's first token,
   // where every item starts) visible to each DFS query; NULL: all of them.
   const int32_t* qlimit;
+  // tcgen05 items scheduled onto a fixed number of CTAs: CTA c runs items
+  // tc_order[tc_cta_begin[c] .. tc_cta_begin[c + 1]) in turn (NULL: one item
+  // per CTA, item blockIdx.x).
+  const int32_t* tc_order;
+  const int32_t* tc_cta_begin;
   // flat mode
   const int32_t* page_indptr;
   const int32_t* num_tokens;

@@ -92,6 +92,30 @@ static int row_tile_for(int kind) {
 // planner needs no device.
 constexpr int kPlanSms = 148;
 
+// Cost model of the two attention kernels that share the GPU during a
+// cascade decode (measured on B200 at 1965 MHz; only used to split the SMs
+// between them and to size split-K chunks):
+//  - tcgen05 kernel: one 128-token tile of one 128-row sub-tile (three
+//    128x128x16 products per 16 tokens and its softmax) per SM, plus a fixed
+//    cost per work item (Q load, pipeline fill, epilogue);
+//  - streaming kernel: stored K/V bytes per SM per ns (bf16: ~50 GB/s per SM;
+//    FP8 pages are widened in registers and run issue-bound), and the HBM
+//    random-page rate it cannot exceed with every SM.
+static double tc_tile_ns(int kv_dtype) {
+  return kv_dtype == DD_DTYPE_BF16 ? 1720.0 : kv_dtype == DD_DTYPE_E4M3 ? 2000.0 : 2200.0;
+}
+constexpr double kTcItemNs = 3000.0;
+static double stream_sm_gbs(int kv_dtype) {
+  return kv_dtype == DD_DTYPE_BF16 ? 50.0 : kv_dtype == DD_DTYPE_E4M3 ? 15.0 : 13.5;
+}
+constexpr double kStreamHbmGbs = 5500.0;
+
+// ns of one SM for a tcgen05 item of `npages` pages and `nrows` rows.
+static double tc_item_ns(int kv_dtype, int64_t npages, int64_t nrows) {
+  const int64_t tiles = (npages + 7) / 8;
+  return (double)tiles * (nrows > 128 ? 2 : 1) * tc_tile_ns(kv_dtype) + kTcItemNs;
+}
+
 // A radix-tree node: a run [off, off + len) of one source table.
 struct Run {
   int32_t q, off, len;          // source table and run within it
@@ -125,6 +149,10 @@ static void reset_plan(dd_plan* p) {
   p->max_depth = 0;
   p->causal = false;
   p->qlimit.clear();
+  p->tc_ctas = 0;
+  p->tc_order.clear();
+  p->tc_cta_begin.clear();
+  p->tc_step_ns = 0.0;
   p->device_base = nullptr;
   p->device_id = -1;
   if (!p->scratch) p->scratch = new PlanScratch();
@@ -301,6 +329,80 @@ static int build_nodes(dd_plan* p, const int32_t* indptr, const uint32_t* ids,
   return DD_OK;
 }
 
+// Schedules the tcgen05 items onto tc_ctas CTAs, longest first onto the
+// least-loaded CTA. The CTA count is the one that finishes the tcgen05 work
+// in the step's time budget, leaving the other SMs to the streaming kernel,
+// which runs concurrently and also takes each tcgen05 CTA's SM when it
+// finishes.
+static void schedule_tc(dd_plan* p) {
+  p->tc_ctas = 0;
+  p->tc_order.clear();
+  p->tc_cta_begin.clear();
+  const std::vector<WorkItem>& items = p->items[kItemTc];
+  const int n = (int)items.size();
+  if (n == 0 || p->opts.tc_sms < 0) return;
+  const int kv = p->cfg.kv_dtype;
+  std::vector<double> cost(n);
+  double total = 0.0;
+  for (int i = 0; i < n; ++i) {
+    cost[i] = tc_item_ns(kv, items[i].npages, items[i].nrows & kItemRowsMask);
+    total += cost[i];
+  }
+  // Items are in decreasing size within each node and nodes in decreasing
+  // item size, so assigning them in order to the least-loaded CTA is the
+  // longest-processing-time rule. Returns the makespan.
+  std::vector<std::pair<double, int32_t>> heap;
+  std::vector<int32_t> cta(n);
+  auto later = [](const std::pair<double, int32_t>& x, const std::pair<double, int32_t>& y) {
+    return x.first > y.first || (x.first == y.first && x.second > y.second);
+  };
+  auto lpt = [&](int K) {
+    heap.clear();
+    for (int c = 0; c < K; ++c) heap.push_back({0.0, c});
+    double span = 0.0;
+    for (int i = 0; i < n; ++i) {
+      std::pop_heap(heap.begin(), heap.end(), later);
+      auto& h = heap.back();
+      cta[i] = h.second;
+      h.first += cost[i];
+      span = std::max(span, h.first);
+      std::push_heap(heap.begin(), heap.end(), later);
+    }
+    return span;
+  };
+  const int kmax = std::min(n, kPlanSms);
+  int K;
+  if (p->opts.tc_sms > 0) {
+    K = std::min(p->opts.tc_sms, kmax);
+  } else {
+    // Enough CTAs to finish the tcgen05 work within the step's budget; equal
+    // items come in whole rounds, so a few larger counts are tried and the
+    // one with the shortest step (budget or makespan) kept.
+    const double step = std::max(p->tc_step_ns, 1.0);
+    const int k0 = std::max(1, std::min(kmax, (int)std::ceil(total / step - 1e-9)));
+    K = k0;
+    double best = std::max(step, lpt(k0));
+    const int inc = std::max(1, (kmax - k0 + 7) / 8);
+    for (int k = k0 + inc; best > step * 1.02 && k <= kmax; k = std::min(k + inc, kmax)) {
+      const double t = std::max(step, lpt(k));
+      if (t < best * 0.99) {
+        best = t;
+        K = k;
+      }
+      if (k == kmax) break;
+    }
+  }
+  lpt(K);
+  std::vector<int32_t>& begin = p->tc_cta_begin;
+  begin.assign((size_t)K + 1, 0);
+  for (int i = 0; i < n; ++i) ++begin[cta[i] + 1];
+  for (int c = 0; c < K; ++c) begin[c + 1] += begin[c];
+  p->tc_order.resize(n);
+  std::vector<int32_t> fill(begin.begin(), begin.end() - 1);
+  for (int i = 0; i < n; ++i) p->tc_order[fill[cta[i]]++] = i;
+  p->tc_ctas = K;
+}
+
 static void build_items(dd_plan* p) {
   const dd_attn_config& c = p->cfg;
   const int Hq = c.num_qo_heads, Hkv = c.num_kv_heads, g = Hq / Hkv, D = c.head_dim;
@@ -314,6 +416,28 @@ static void build_items(dd_plan* p) {
   sc.keys.resize(N);
   sc.qcount.assign((size_t)B + 1, 0);  // difference array, then path lengths
   int64_t n_items[kNumItemKinds] = {0, 0, 0, 0};
+  // Time budget of the step (ns) from the cost model: the tcgen05 work and
+  // the streaming work share the SMs, and the stream cannot beat HBM. The
+  // tcgen05 nodes are then cut into items of at most a quarter of it, so
+  // their schedule onto part of the SMs balances.
+  const bool tc_sched = p->opts.tc_sms >= 0;
+  double tc_ns = 0.0, st_sm_ns = 0.0, st_bytes = 0.0;
+  for (size_t ni = 0; ni < N; ++ni) {
+    const Node& n = p->nodes[ni];
+    const int64_t rows = (int64_t)n.num_q * g;
+    const int kind = kind_for(c, p->opts, rows);
+    const double bytes = (double)n.page_count * 2 * kPageSize * D * elem * Hkv;
+    if (kind == kItemTc) {
+      const int64_t full = rows / 256, rest = rows % 256;
+      tc_ns += (double)Hkv * (full * (tc_item_ns(c.kv_dtype, n.page_count, 256) - kTcItemNs) +
+                              (rest ? tc_item_ns(c.kv_dtype, n.page_count, rest) - kTcItemNs : 0.0));
+    } else if (kind == kItemMma) {
+      st_sm_ns += bytes * (double)((rows + 15) / 16) / stream_sm_gbs(c.kv_dtype);
+      st_bytes += bytes;
+    }
+  }
+  const double step_ns = std::max((tc_ns + st_sm_ns) / kPlanSms, st_bytes / kStreamHbmGbs);
+  p->tc_step_ns = step_ns;
   // Pass 1: kernel kind, split-K chunk count and slots of every node.
   p->num_slots = 0;
   for (size_t ni = 0; ni < N; ++ni) {
@@ -334,7 +458,14 @@ static void build_items(dd_plan* p) {
     int64_t chunk_pages = p->opts.max_chunk_pages > 0 ? p->opts.max_chunk_pages
                           : (row_tiles == 1 ? 16 : (int64_t)1 << 30);
     int64_t k = std::min<int64_t>(kmax, (n.page_count + chunk_pages - 1) / chunk_pages);
-    if ((kind == kItemTc || kind == kItemTc2) && p->opts.max_chunk_pages <= 0) {
+    if (kind == kItemTc && tc_sched && p->opts.max_chunk_pages <= 0) {
+      // Scheduled tcgen05 items: chunks of at most a quarter of the step's
+      // budget (at least 32 pages, at most 8 chunks) so the longest-first
+      // schedule onto the tcgen05 CTAs comes out even.
+      const double item = tc_item_ns(c.kv_dtype, n.page_count, std::min<int64_t>(rows, rt));
+      const int64_t want = (int64_t)std::ceil(item / std::max(step_ns / 4.0, 1.0));
+      k = std::max<int64_t>(1, std::min<int64_t>({want, 8, std::max<int64_t>(1, n.page_count / 32)}));
+    } else if ((kind == kItemTc || kind == kItemTc2) && p->opts.max_chunk_pages <= 0) {
       // Wide nodes are compute-bound: split their pages so the tensor-core
       // grid covers the SMs (at least 32 pages per chunk), even though each
       // chunk adds a partial state per row (at most 4 chunks, unless fewer
@@ -426,6 +557,7 @@ static void build_items(dd_plan* p) {
         }
     }
   }
+  schedule_tc(p);
   // Deepest node of every DFS query (nodes are in pre-order, so a node's
   // descendants come after it); pages in use.
   p->q_leaf.assign((size_t)B, -1);
@@ -451,6 +583,8 @@ static void pack_image(dd_plan* p) {
   p->off_pindptr = take(p->path_indptr.size() * sizeof(int32_t));
   p->off_pslots = take(p->path_slots.size() * sizeof(int32_t));
   p->off_qlimit = take(p->qlimit.size() * sizeof(int32_t));
+  p->off_tc_order = take(p->tc_order.size() * sizeof(int32_t));
+  p->off_tc_cta_begin = take(p->tc_cta_begin.size() * sizeof(int32_t));
   // Reused across rebuilds; alignment gaps are never read.
   p->image.resize(std::max<size_t>(off, kAlign));
   auto put = [&](size_t o, const void* src, size_t n) {
@@ -463,6 +597,8 @@ static void pack_image(dd_plan* p) {
   put(p->off_pindptr, p->path_indptr.data(), p->path_indptr.size() * 4);
   put(p->off_pslots, p->path_slots.data(), p->path_slots.size() * 4);
   put(p->off_qlimit, p->qlimit.data(), p->qlimit.size() * 4);
+  put(p->off_tc_order, p->tc_order.data(), p->tc_order.size() * 4);
+  put(p->off_tc_cta_begin, p->tc_cta_begin.data(), p->tc_cta_begin.size() * 4);
 }
 
 }  // namespace dd
@@ -498,7 +634,7 @@ int dd_plan_create(const dd_attn_config* cfg, int32_t batch_size, const int32_t*
   if (opts) {
     p->opts = *opts;
   } else {
-    p->opts = dd_plan_options{1, 0, 1, 0};
+    p->opts = dd_plan_options{1, 0, 1, 0, 0};
   }
   p->batch_size = batch_size;
   try {
@@ -587,7 +723,7 @@ int dd_plan_create_prefill(const dd_attn_config* cfg, int32_t num_seqs, const in
   if (!p) return fail(DD_ERR_ALLOCATION, "host allocation failed");
   p->cfg = *cfg;
   if (p->cfg.scale <= 0.f) p->cfg.scale = 1.0f / std::sqrt((float)cfg->head_dim);
-  p->opts = opts ? *opts : dd_plan_options{1, 0, 1, 0};
+  p->opts = opts ? *opts : dd_plan_options{1, 0, 1, 0, 0};
   p->opts.cta_pairs = 0;  // the CTA-pair kernel has no causal mask
   try {
     reset_plan(p);
@@ -759,6 +895,7 @@ int dd_plan_get_info(const dd_plan* p, dd_plan_info* info) {
   info->kv_tokens_flat = p->kv_tokens_flat;
   for (int k = 0; k < kNumItemKinds; ++k) info->kv_tokens_by_kernel[k] = p->kv_tokens_by_kind[k];
   info->tc_row_tokens = p->tc_row_tokens;
+  info->tc_ctas = p->tc_ctas > 0 ? p->tc_ctas : (int32_t)p->items[kItemTc].size();
   info->workspace_bytes = plan_workspace_bytes(p);
   info->device_bytes = p->image.size();
   return DD_OK;

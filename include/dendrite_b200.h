@@ -128,6 +128,9 @@ typedef struct dd_plan_options {
   int32_t use_tensor_cores;/* 1 (default): tcgen05 path for nodes with many rows */
   int32_t cta_pairs;        /* 1: nodes of > 256 rows run on CTA pairs (cta_group::2
                              * tcgen05 kernel, bf16 only); 0 (default): one-SM kernel */
+  int32_t tc_sms;           /* SMs given to the tcgen05 kernel while the streaming kernel
+                             * runs on the others: 0 (default) = from the plan's cost
+                             * model; N > 0 = N; -1 = one CTA per tcgen05 work item */
 } dd_plan_options;
 
 typedef struct dd_plan_info {
@@ -147,6 +150,7 @@ typedef struct dd_plan_info {
   /* Sum over tcgen05 nodes and KV heads of (query rows x tokens): the
    * kernel's 4 * head_dim FLOPs per unit (Q.K^T and P.V). */
   int64_t tc_row_tokens;
+  int32_t tc_ctas;         /* CTAs of the tcgen05 launch (0: no tcgen05 work) */
 } dd_plan_info;
 
 int dd_plan_create(const dd_attn_config* cfg, int32_t batch_size,
