@@ -744,8 +744,8 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="mcts8b")
     ap.add_argument("--cpu-budget", type=float, default=10.0)
     ap.add_argument("--tc-sms", type=int, default=0,
-                    help="SMs of the tcgen05 kernel while the streaming kernel runs (plan option "
-                         "tc_sms: 0 = cost model, -1 = one CTA per item)")
+                    help="CTAs of the tcgen05 kernel (plan option tc_sms: 0 = one per SM, "
+                         "-1 = one CTA per work item)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--clocks-csv", default=None,
                     help="also write the raw nvidia-smi clock samples of the timed region here")

@@ -357,6 +357,29 @@ __global__ void __launch_bounds__(TcCfg<KV>::kThreads, 1)
     const float scale_log2 = a.scale_log2;
     int seen = 0;   // tiles of this sub-tile handed over so far (s_full / p_full phase)
     int done = 0;   // items with products so far (item_done phase)
+    // Address of this thread's query row of item `iq` (NULL for a dead row).
+    auto q_row = [&](const WorkItem& iq) -> const uint4* {
+      if (row >= (iq.nrows & kItemRowsMask)) return nullptr;
+      const int rr = iq.row0 + row, qi = rr / a.g;
+      const int hq = qo_head_of(a.gqa_map, iq.kv_head, rr % a.g, a.Hkv, a.g);
+      const int qid = a.qorder ? a.qorder[iq.q_begin + qi] : iq.q_begin + qi;
+      return reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(a.q) +
+                                            ((size_t)qid * a.Hq + hq) * 128);
+    };
+    // Q row -> the sub-tile's 128-byte-swizzled K-major tile, then hand the
+    // tile to the MMA warp (the previous item's products are complete).
+    auto write_q = [&](const WorkItem& iq) {
+      const uint4* src = q_row(iq);
+      uint8_t* qx = q_s + x * kTcQBytes + r * 128;
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        const uint4 v = src ? src[c] : make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4*>(qx + (c >> 3) * (kTcQBytes / 2) + (((c & 7) ^ (r & 7)) << 4)) = v;
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(&bars.q_ready);
+    };
+    if (ib < ie) write_q(tc_item(a, ib));
     for (int ii = ib; ii < ie; ++ii) {
       WorkItem it = tc_item(a, ii);
       const bool causal = (it.nrows & kItemCausal) != 0;
@@ -365,25 +388,13 @@ __global__ void __launch_bounds__(TcCfg<KV>::kThreads, 1)
       const int ntiles = (npages + kTcPagesPerTile - 1) / kTcPagesPerTile;
       const bool live = row < it.nrows;
       const bool active = x == 0 || it.nrows > 128;
-      // Q row -> the sub-tile's 128-byte-swizzled K-major tile. The previous
-      // item's products are complete (its item_done was awaited below).
-      {
-        const uint4* src = nullptr;
-        if (live) {
-          const int rr = it.row0 + row, qi = rr / a.g;
-          const int hq = qo_head_of(a.gqa_map, it.kv_head, rr % a.g, a.Hkv, a.g);
-          const int qid = a.qorder ? a.qorder[it.q_begin + qi] : it.q_begin + qi;
-          src = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(a.q) +
-                                               ((size_t)qid * a.Hq + hq) * 128);
+      if (ii + 1 < ie) {
+        // The next item's query row into L2 while this item runs.
+        const uint4* nq = q_row(tc_item(a, ii + 1));
+        if (nq) {
+          asm volatile("prefetch.global.L2 [%0];" ::"l"(nq));
+          asm volatile("prefetch.global.L2 [%0];" ::"l"(nq + 8));
         }
-        uint8_t* qx = q_s + x * kTcQBytes + r * 128;
-#pragma unroll
-        for (int c = 0; c < 16; ++c) {
-          const uint4 v = live ? src[c] : make_uint4(0, 0, 0, 0);
-          *reinterpret_cast<uint4*>(qx + (c >> 3) * (kTcQBytes / 2) + (((c & 7) ^ (r & 7)) << 4)) = v;
-        }
-        fence_proxy_async_smem();
-        mbar_arrive(&bars.q_ready);
       }
       // Causal plans: tokens of the node this row sees (items start at the
       // node's first token).
@@ -477,6 +488,11 @@ __global__ void __launch_bounds__(TcCfg<KV>::kThreads, 1)
         ++done;
         tc_fence_after();
       }
+      // The next item's Q goes in before this epilogue, so its first
+      // products overlap it (they write S; its first P.V, which overwrites
+      // O, waits for this warp's P of that item, which comes after the
+      // epilogue has read O).
+      if (ii + 1 < ie && __all_sync(0xffffffffu, ok)) write_q(tc_item(a, ii + 1));
       // Epilogue: the normalised O row and its LSE.
       if (active) {
         const float L = f2_lo(lsum) + f2_hi(lsum);
@@ -507,7 +523,7 @@ __global__ void __launch_bounds__(TcCfg<KV>::kThreads, 1)
         if (live) a.part_lse[slot] = L > 0.f ? m_used + log2f(L) : -INFINITY;
       }
       // O was read (tcgen05.wait::ld above) before this warp hands over the
-      // next item's Q, whose first P.V overwrites O.
+      // next item's first P, after which P.V overwrites O.
       tc_fence_before();
       if (!__all_sync(0xffffffffu, ok)) break;
     }

@@ -111,11 +111,9 @@ struct dd_plan {
   std::vector<uint8_t> image;
   size_t off_items[dd::kNumItemKinds] = {0, 0, 0, 0, 0};
   size_t off_pages = 0, off_qorder = 0, off_pindptr = 0, off_pslots = 0;
-  // Schedule of the tcgen05 items onto tc_ctas CTAs (the rest of the SMs run
-  // the streaming kernel meanwhile): CTA c runs items
+  // Schedule of the tcgen05 items onto tc_ctas CTAs: CTA c runs items
   // tc_order[tc_cta_begin[c] .. tc_cta_begin[c + 1]).
   int32_t tc_ctas = 0;
-  double tc_step_ns = 0.0;  // the cost model's step time (planning only)
   std::vector<int32_t> tc_order, tc_cta_begin;
   size_t off_tc_order = 0, off_tc_cta_begin = 0;
   // Set by dd_plan_upload.

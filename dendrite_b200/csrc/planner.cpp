@@ -92,29 +92,32 @@ static int row_tile_for(int kind) {
 // planner needs no device.
 constexpr int kPlanSms = 148;
 
-// Cost model of the two attention kernels that share the GPU during a
-// cascade decode (measured on B200 at 1965 MHz; only used to split the SMs
-// between them and to size split-K chunks):
-//  - tcgen05 kernel: one 128-token tile of one 128-row sub-tile (three
-//    128x128x16 products per 16 tokens and its softmax) per SM, plus a fixed
-//    cost per work item (Q load, pipeline fill, epilogue);
-//  - streaming kernel: stored K/V bytes per SM per ns (bf16: ~50 GB/s per SM;
-//    FP8 pages are widened in registers and run issue-bound), and the HBM
-//    random-page rate it cannot exceed with every SM.
+// Cost model of the tcgen05 kernel (measured on B200 at 1965 MHz; only used
+// to size split-K chunks and to schedule items onto CTAs): one 128-token
+// tile of one 128-row sub-tile (three 128x128x16 products per 16 tokens and
+// its softmax) per SM, plus a fixed cost per work item (Q load, pipeline
+// fill, epilogue).
 static double tc_tile_ns(int kv_dtype) {
   return kv_dtype == DD_DTYPE_BF16 ? 1720.0 : kv_dtype == DD_DTYPE_E4M3 ? 2000.0 : 2200.0;
 }
 constexpr double kTcItemNs = 3000.0;
-static double stream_sm_gbs(int kv_dtype) {
-  return kv_dtype == DD_DTYPE_BF16 ? 50.0 : kv_dtype == DD_DTYPE_E4M3 ? 15.0 : 13.5;
-}
-constexpr double kStreamHbmGbs = 5500.0;
-
 // ns of one SM for a tcgen05 item of `npages` pages and `nrows` rows.
 static double tc_item_ns(int kv_dtype, int64_t npages, int64_t nrows) {
   const int64_t tiles = (npages + 7) / 8;
   return (double)tiles * (nrows > 128 ? 2 : 1) * tc_tile_ns(kv_dtype) + kTcItemNs;
 }
+// Split-K chunks of a tcgen05 node so its items take at most cap_ns (at
+// least 32 pages a chunk; at most 8 chunks, or enough
+// for one item per SM when the node has few row tiles x KV heads, as one KV
+// head of a long tree per GPU).
+static int64_t tc_chunks(int kv_dtype, int64_t npages, int64_t nrows, int64_t units, double cap_ns) {
+  const double item = tc_item_ns(kv_dtype, npages, nrows);
+  const int64_t want = cap_ns > 0.0 ? (int64_t)std::ceil(item / cap_ns - 0.05) : 1;
+  const int64_t most = std::max<int64_t>(8, (kPlanSms + units - 1) / std::max<int64_t>(units, 1));
+  return std::max<int64_t>(1, std::min<int64_t>({want, most, std::max<int64_t>(1, npages / 32)}));
+}
+// Partial-state bytes the merge moves per ns (write + read, mostly in L2).
+constexpr double kMergeBytesPerNs = 5000.0;
 
 // A radix-tree node: a run [off, off + len) of one source table.
 struct Run {
@@ -135,6 +138,7 @@ struct PlanScratch {
   };
   std::vector<Frame> stack;
   std::vector<std::pair<int64_t, int32_t>> keys;
+  std::vector<double> sim_cost, sim_load;  // tcgen05 chunk-size search
 };
 
 static void reset_plan(dd_plan* p) {
@@ -152,7 +156,6 @@ static void reset_plan(dd_plan* p) {
   p->tc_ctas = 0;
   p->tc_order.clear();
   p->tc_cta_begin.clear();
-  p->tc_step_ns = 0.0;
   p->device_base = nullptr;
   p->device_id = -1;
   if (!p->scratch) p->scratch = new PlanScratch();
@@ -329,11 +332,10 @@ static int build_nodes(dd_plan* p, const int32_t* indptr, const uint32_t* ids,
   return DD_OK;
 }
 
-// Schedules the tcgen05 items onto tc_ctas CTAs, longest first onto the
-// least-loaded CTA. The CTA count is the one that finishes the tcgen05 work
-// in the step's time budget, leaving the other SMs to the streaming kernel,
-// which runs concurrently and also takes each tcgen05 CTA's SM when it
-// finishes.
+// Schedules the tcgen05 items onto tc_ctas CTAs (one per SM, or the
+// plan's tc_sms), longest first onto the least-loaded CTA. The streaming
+// kernel, launched after it as a programmatic dependent, starts on the SMs
+// left free and takes each tcgen05 CTA's SM when that CTA finishes.
 static void schedule_tc(dd_plan* p) {
   p->tc_ctas = 0;
   p->tc_order.clear();
@@ -343,11 +345,7 @@ static void schedule_tc(dd_plan* p) {
   if (n == 0 || p->opts.tc_sms < 0) return;
   const int kv = p->cfg.kv_dtype;
   std::vector<double> cost(n);
-  double total = 0.0;
-  for (int i = 0; i < n; ++i) {
-    cost[i] = tc_item_ns(kv, items[i].npages, items[i].nrows & kItemRowsMask);
-    total += cost[i];
-  }
+  for (int i = 0; i < n; ++i) cost[i] = tc_item_ns(kv, items[i].npages, items[i].nrows & kItemRowsMask);
   // Items are in decreasing size within each node and nodes in decreasing
   // item size, so assigning them in order to the least-loaded CTA is the
   // longest-processing-time rule. Returns the makespan.
@@ -370,28 +368,7 @@ static void schedule_tc(dd_plan* p) {
     }
     return span;
   };
-  const int kmax = std::min(n, kPlanSms);
-  int K;
-  if (p->opts.tc_sms > 0) {
-    K = std::min(p->opts.tc_sms, kmax);
-  } else {
-    // Enough CTAs to finish the tcgen05 work within the step's budget; equal
-    // items come in whole rounds, so a few larger counts are tried and the
-    // one with the shortest step (budget or makespan) kept.
-    const double step = std::max(p->tc_step_ns, 1.0);
-    const int k0 = std::max(1, std::min(kmax, (int)std::ceil(total / step - 1e-9)));
-    K = k0;
-    double best = std::max(step, lpt(k0));
-    const int inc = std::max(1, (kmax - k0 + 7) / 8);
-    for (int k = k0 + inc; best > step * 1.02 && k <= kmax; k = std::min(k + inc, kmax)) {
-      const double t = std::max(step, lpt(k));
-      if (t < best * 0.99) {
-        best = t;
-        K = k;
-      }
-      if (k == kmax) break;
-    }
-  }
+  const int K = std::max(1, std::min({p->opts.tc_sms > 0 ? p->opts.tc_sms : kPlanSms, n, kPlanSms}));
   lpt(K);
   std::vector<int32_t>& begin = p->tc_cta_begin;
   begin.assign((size_t)K + 1, 0);
@@ -416,28 +393,63 @@ static void build_items(dd_plan* p) {
   sc.keys.resize(N);
   sc.qcount.assign((size_t)B + 1, 0);  // difference array, then path lengths
   int64_t n_items[kNumItemKinds] = {0, 0, 0, 0};
-  // Time budget of the step (ns) from the cost model: the tcgen05 work and
-  // the streaming work share the SMs, and the stream cannot beat HBM. The
-  // tcgen05 nodes are then cut into items of at most a quarter of it, so
-  // their schedule onto part of the SMs balances.
+  // Split-K cap of the scheduled tcgen05 items: the largest node's item
+  // time over k = 1, 2, ... chunks, whichever gives the shortest
+  // longest-first schedule plus the merge's extra partial states (written
+  // and read once more per chunk). Equal items come in whole rounds, so finer
+  // chunks only pay when they even out the last round.
   const bool tc_sched = p->opts.tc_sms >= 0;
-  double tc_ns = 0.0, st_sm_ns = 0.0, st_bytes = 0.0;
-  for (size_t ni = 0; ni < N; ++ni) {
-    const Node& n = p->nodes[ni];
-    const int64_t rows = (int64_t)n.num_q * g;
-    const int kind = kind_for(c, p->opts, rows);
-    const double bytes = (double)n.page_count * 2 * kPageSize * D * elem * Hkv;
-    if (kind == kItemTc) {
-      const int64_t full = rows / 256, rest = rows % 256;
-      tc_ns += (double)Hkv * (full * (tc_item_ns(c.kv_dtype, n.page_count, 256) - kTcItemNs) +
-                              (rest ? tc_item_ns(c.kv_dtype, n.page_count, rest) - kTcItemNs : 0.0));
-    } else if (kind == kItemMma) {
-      st_sm_ns += bytes * (double)((rows + 15) / 16) / stream_sm_gbs(c.kv_dtype);
-      st_bytes += bytes;
+  double tc_cap_ns = 0.0;
+  if (tc_sched && p->opts.max_chunk_pages <= 0) {
+    double item_max = 0.0;
+    for (size_t ni = 0; ni < N; ++ni) {
+      const Node& n = p->nodes[ni];
+      const int64_t rows = (int64_t)n.num_q * g;
+      if (kind_for(c, p->opts, rows) != kItemTc) continue;
+      item_max = std::max(item_max, tc_item_ns(c.kv_dtype, n.page_count, std::min<int64_t>(rows, 256)));
+    }
+    const int K = p->opts.tc_sms > 0 ? p->opts.tc_sms : kPlanSms;
+    double best = 0.0;
+    std::vector<double>& cost = sc.sim_cost;
+    std::vector<double>& load = sc.sim_load;
+    size_t prev_n = 0;
+    for (int R : {1, 2, 3, 4, 5, 6, 8, 12, 16, 24}) {
+      if (item_max <= 0.0) break;
+      const double cap = item_max / R * 1.0001;
+      cost.clear();
+      double merge_bytes = 0.0;
+      for (size_t ni = 0; ni < N; ++ni) {
+        const Node& n = p->nodes[ni];
+        const int64_t rows = (int64_t)n.num_q * g;
+        if (kind_for(c, p->opts, rows) != kItemTc) continue;
+        const int64_t k = tc_chunks(c.kv_dtype, n.page_count, std::min<int64_t>(rows, 256),
+                                    (rows + 255) / 256 * Hkv, cap);
+        merge_bytes += (double)(k - 1) * n.num_q * Hq * (D + 1) * 4.0 * 2.0;
+        for (int64_t t = 0; t * 256 < rows; ++t) {
+          const double ci = tc_item_ns(c.kv_dtype, (n.page_count + k - 1) / k, std::min<int64_t>(256, rows - t * 256));
+          for (int64_t r = 0; r < k * Hkv; ++r) cost.push_back(ci);
+        }
+      }
+      if (cost.size() == prev_n) continue;  // the chunk caps bind: same split as before
+      prev_n = cost.size();
+      std::sort(cost.begin(), cost.end(), std::greater<double>());
+      const int kc = std::max(1, std::min<int>(K, (int)cost.size()));
+      // Loads of the CTAs as a min-heap (negated for std's max-heap).
+      load.assign(kc, 0.0);
+      double span = 0.0;
+      for (double ci : cost) {
+        std::pop_heap(load.begin(), load.end());
+        load.back() -= ci;
+        span = std::max(span, -load.back());
+        std::push_heap(load.begin(), load.end());
+      }
+      const double t = span + merge_bytes / kMergeBytesPerNs;
+      if (R == 1 || t < best * 0.98) {
+        best = t;
+        tc_cap_ns = cap;
+      }
     }
   }
-  const double step_ns = std::max((tc_ns + st_sm_ns) / kPlanSms, st_bytes / kStreamHbmGbs);
-  p->tc_step_ns = step_ns;
   // Pass 1: kernel kind, split-K chunk count and slots of every node.
   p->num_slots = 0;
   for (size_t ni = 0; ni < N; ++ni) {
@@ -459,12 +471,8 @@ static void build_items(dd_plan* p) {
                           : (row_tiles == 1 ? 16 : (int64_t)1 << 30);
     int64_t k = std::min<int64_t>(kmax, (n.page_count + chunk_pages - 1) / chunk_pages);
     if (kind == kItemTc && tc_sched && p->opts.max_chunk_pages <= 0) {
-      // Scheduled tcgen05 items: chunks of at most a quarter of the step's
-      // budget (at least 32 pages, at most 8 chunks) so the longest-first
-      // schedule onto the tcgen05 CTAs comes out even.
-      const double item = tc_item_ns(c.kv_dtype, n.page_count, std::min<int64_t>(rows, rt));
-      const int64_t want = (int64_t)std::ceil(item / std::max(step_ns / 4.0, 1.0));
-      k = std::max<int64_t>(1, std::min<int64_t>({want, 8, std::max<int64_t>(1, n.page_count / 32)}));
+      // Scheduled tcgen05 items: the chunk count of the chosen time cap.
+      k = tc_chunks(c.kv_dtype, n.page_count, std::min<int64_t>(rows, rt), row_tiles * Hkv, tc_cap_ns);
     } else if ((kind == kItemTc || kind == kItemTc2) && p->opts.max_chunk_pages <= 0) {
       // Wide nodes are compute-bound: split their pages so the tensor-core
       // grid covers the SMs (at least 32 pages per chunk), even though each

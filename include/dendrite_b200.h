@@ -128,9 +128,10 @@ typedef struct dd_plan_options {
   int32_t use_tensor_cores;/* 1 (default): tcgen05 path for nodes with many rows */
   int32_t cta_pairs;        /* 1: nodes of > 256 rows run on CTA pairs (cta_group::2
                              * tcgen05 kernel, bf16 only); 0 (default): one-SM kernel */
-  int32_t tc_sms;           /* SMs given to the tcgen05 kernel while the streaming kernel
-                             * runs on the others: 0 (default) = from the plan's cost
-                             * model; N > 0 = N; -1 = one CTA per tcgen05 work item */
+  int32_t tc_sms;           /* CTAs of the tcgen05 kernel, each running a scheduled list
+                             * of work items: 0 (default) = one per SM; N > 0 = N (the
+                             * streaming kernel starts on the other SMs); -1 = one CTA
+                             * per work item with the older split-K rule */
 } dd_plan_options;
 
 typedef struct dd_plan_info {
