@@ -3,7 +3,9 @@
 // root and upper nodes of a tree, where hundreds to thousands of (query, GQA
 // head) rows read the same pages.
 //
-// One CTA per work item = (node, KV head, 256-row tile, page range). The rows
+// A work item is (node, KV head, 256-row tile, page range); each CTA runs the
+// list the plan scheduled onto it (or one item, blockIdx.x), carrying the K/V
+// ring, the barrier phases and its TMEM over from item to item. The rows
 // form two 128-row sub-tiles A and B that share every K/V tile:
 //   warp 0      TMA producer: K and V tiles of 128 tokens (8 pages x 2 boxes
 //               of [16 tokens][64 dims], 128-byte swizzle) into the K/V

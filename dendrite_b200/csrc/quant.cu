@@ -32,8 +32,40 @@ __device__ __forceinline__ void load8(const void* src, int src_dtype, size_t i, 
   }
 }
 
-// Vectors (8 elements) per thread per round: their loads are issued
-// before any is used.
+// Pass 1 of per-head E4M3: amax per (K/V, KV head) over the whole pool.
+// One warp per page slice ([16][D] elements of one (page, K/V, head)); a
+// lane's D/16 16-byte loads of a slice are issued together.
+template <int D>
+__global__ void amax_per_head_kernel(const void* src, int src_dtype, int64_t nslices, int Hkv,
+                                     uint32_t* amax_bits) {
+  __shared__ uint32_t sm[64];
+  const int n2 = 2 * Hkv;
+  for (int i = threadIdx.x; i < n2; i += blockDim.x) sm[i] = 0;
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const int64_t warp0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  constexpr int per = kPageSize * D, kLoads = per / (32 * 8);
+  for (int64_t s = warp0; s < nslices; s += nwarps) {
+    float v[kLoads][8];
+#pragma unroll
+    for (int u = 0; u < kLoads; ++u) load8(src, src_dtype, (size_t)s * per + (u * 32 + lane) * 8, v[u]);
+    float m = 0.f;
+#pragma unroll
+    for (int u = 0; u < kLoads; ++u)
+#pragma unroll
+      for (int k = 0; k < 8; ++k) m = fmaxf(m, fabsf(v[u][k]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) atomicMax(&sm[(uint32_t)s % (uint32_t)n2], __float_as_uint(m));
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < n2; i += blockDim.x)
+    if (sm[i]) atomicMax(&amax_bits[i], sm[i]);
+}
+
+// Vectors (8 elements) per thread per round of the quantize kernels: their
+// loads are issued before any is converted.
 constexpr int kQuantUnroll = 4;
 
 __device__ __forceinline__ float head_scale_from_amax(float amax, int mode) {
@@ -41,93 +73,21 @@ __device__ __forceinline__ float head_scale_from_amax(float amax, int mode) {
   return mode == 0 ? amax * (float)(1.0 / 448.0) : __fdiv_rn(amax, 448.f);
 }
 
-// Workspace of the per-head E4M3 quantizer: the amax bits of each
-// (K/V, KV head) and the grid barrier's arrival count (zeroed per call).
-struct QuantWs {
-  uint32_t amax_bits[64];
-  uint32_t arrived;
-  uint32_t timed_out;  // nonzero: the barrier gave up and no code was written
-  uint32_t pad[62];
-};
-static_assert(sizeof(QuantWs) == 2 * kAlign, "quant workspace");
-
-// Per-head E4M3 in one cooperative launch (all CTAs resident):
-//  1. amax per (K/V, head) over the CTA's share of the pool (grid-stride
-//     vectors; a warp's 32 consecutive vectors lie in one page slice, so one
-//     shared atomic per warp and round), merged into the workspace;
-//  2. a grid barrier (bounded wait);
-//  3. codes = E4M3_rn_sat(x / scale[kv][h]) over the same share, whose bytes
-//     were just read and are mostly still in L2 (the pool of a decode
-//     batch's pages is far smaller than the 126 MB L2); CTA 0 also stores
-//     the scales.
-__global__ void __launch_bounds__(256) quant_e4m3_kernel(const void* src, int src_dtype,
-                                                         int64_t nelem, int Hkv, int D,
-                                                         QuantWs* ws, int mode, uint8_t* codes,
-                                                         float* scales) {
-  __shared__ uint32_t sm[64];
+// Pass 2: codes = E4M3_rn_sat(x / scale[kv][h]); block 0 also stores scales.
+__global__ void quant_e4m3_kernel(const void* src, int src_dtype, int64_t nelem, int Hkv, int D,
+                                  const uint32_t* amax_bits, int mode, uint8_t* codes,
+                                  float* scales) {
   __shared__ float ssc[64];
-  __shared__ int go;
   const int n2 = 2 * Hkv;
-  for (int i = threadIdx.x; i < n2; i += blockDim.x) sm[i] = 0;
-  __syncthreads();
-  const int lane = threadIdx.x & 31;
-  const int vec_shift = 31 - __clz(kPageSize * D / 8);  // vectors per page slice = 2 D
-  const int64_t nvec = nelem / 8;
-  const int64_t step = (int64_t)gridDim.x * blockDim.x * kQuantUnroll;
-  const int64_t first = (int64_t)blockIdx.x * blockDim.x * kQuantUnroll;
-  for (int64_t base = first; base < nvec; base += step) {
-    float x[kQuantUnroll][8];
-#pragma unroll
-    for (int u = 0; u < kQuantUnroll; ++u) {
-      const int64_t v = base + u * blockDim.x + threadIdx.x;
-      load8(src, src_dtype, (size_t)(v < nvec ? v : 0) * 8, x[u]);
-    }
-#pragma unroll
-    for (int u = 0; u < kQuantUnroll; ++u) {
-      const int64_t v = base + u * blockDim.x + threadIdx.x;
-      float m = 0.f;
-      if (v < nvec)
-#pragma unroll
-        for (int k = 0; k < 8; ++k) m = fmaxf(m, fabsf(x[u][k]));
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-      const int64_t v0 = base + u * blockDim.x + (threadIdx.x & ~31);
-      if (lane == 0 && v0 < nvec && m > 0.f)
-        atomicMax(&sm[(uint32_t)(v0 >> vec_shift) % (uint32_t)n2], __float_as_uint(m));
-    }
-  }
-  __syncthreads();
   for (int i = threadIdx.x; i < n2; i += blockDim.x)
-    if (sm[i]) atomicMax(&ws->amax_bits[i], sm[i]);
-  // Grid barrier: every CTA's amax is in before any scale is derived.
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence();
-    atomicAdd(&ws->arrived, 1u);
-    const uint64_t t0 = global_ns();
-    int ok = 1;
-    for (uint32_t it = 0;; ++it) {
-      uint32_t n;
-      asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(n) : "l"(&ws->arrived) : "memory");
-      if (n >= gridDim.x) break;
-      if ((it & 63u) == 63u && global_ns() - t0 > kWaitLimitNs) {
-        ok = 0;
-        atomicExch(&ws->timed_out, 1u);
-        break;
-      }
-    }
-    go = ok;
-  }
-  __syncthreads();
-  if (!go) return;
-  for (int i = threadIdx.x; i < n2; i += blockDim.x) {
-    const uint32_t bits = *reinterpret_cast<volatile const uint32_t*>(&ws->amax_bits[i]);
-    ssc[i] = head_scale_from_amax(__uint_as_float(bits), mode);
-  }
+    ssc[i] = head_scale_from_amax(__uint_as_float(amax_bits[i]), mode);
   __syncthreads();
   if (blockIdx.x == 0)
     for (int i = threadIdx.x; i < n2; i += blockDim.x) scales[i] = ssc[i];
-  for (int64_t base = first; base < nvec; base += step) {
+  const int vec_shift = 31 - __clz(kPageSize * D / 8);  // vectors per page slice = 2 D
+  const int64_t nvec = nelem / 8;
+  const int64_t step = (int64_t)gridDim.x * blockDim.x * kQuantUnroll;
+  for (int64_t base = (int64_t)blockIdx.x * blockDim.x * kQuantUnroll; base < nvec; base += step) {
     float x[kQuantUnroll][8];
 #pragma unroll
     for (int u = 0; u < kQuantUnroll; ++u) {
@@ -258,7 +218,7 @@ using namespace dd;
 
 extern "C" size_t dd_quantize_workspace_size(const dd_quant_config* qc) {
   if (check_qc(qc)) return 0;
-  return qc->format == DD_DTYPE_E4M3 ? sizeof(QuantWs) : 0;
+  return qc->format == DD_DTYPE_E4M3 ? kAlign : 0;
 }
 
 extern "C" int dd_quantize_kv_pages(const dd_quant_config* qc, const void* src, int64_t num_pages,
@@ -277,25 +237,19 @@ extern "C" int dd_quantize_kv_pages(const dd_quant_config* qc, const void* src, 
   if (qc->format == DD_DTYPE_E4M3) {
     if (!workspace || ws_bytes < dd_quantize_workspace_size(qc))
       return fail(DD_ERR_WORKSPACE, "E4M3 quantization needs dd_quantize_workspace_size bytes");
-    if ((uintptr_t)workspace & 3) return fail(DD_ERR_INVALID_ARGUMENT, "workspace must be 4-byte aligned");
-    QuantWs* qws = reinterpret_cast<QuantWs*>(workspace);
-    cudaError_t e = cudaMemsetAsync(qws, 0, sizeof(QuantWs), st);
+    uint32_t* amax = reinterpret_cast<uint32_t*>(workspace);
+    cudaError_t e = cudaMemsetAsync(amax, 0, sizeof(uint32_t) * 2 * Hkv, st);
     if (e != cudaSuccess) return fail(DD_ERR_CUDA, cudaGetErrorString(e));
-    // Cooperative launch: every CTA resident, so the grid barrier holds.
-    int dev = 0, sms = 148, per_sm = 1;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, quant_e4m3_kernel, 256, 0);
-    if (e != cudaSuccess) return fail(DD_ERR_CUDA, cudaGetErrorString(e));
-    const int64_t need = (nelem / 8 + 256 * kQuantUnroll - 1) / (256 * kQuantUnroll);
-    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(need, (int64_t)sms * std::max(1, std::min(per_sm, 8))));
-    int src_dtype = qc->src_dtype, mode = qc->scale_mode;
-    float* fscales = reinterpret_cast<float*>(scales);
-    void* args[] = {const_cast<void**>(&src), &src_dtype, const_cast<int64_t*>(&nelem),
-                    const_cast<int*>(&Hkv), const_cast<int*>(&D), &qws, &mode, &codes, &fscales};
+    const int64_t nslices = num_pages * 2 * Hkv;
+    { ProfScope ps(kProfQuant, st);
+    const int ga = grid_for(nslices * 32, 256);
+    if (D == 64) amax_per_head_kernel<64><<<ga, 256, 0, st>>>(src, qc->src_dtype, nslices, Hkv, amax);
+    else if (D == 128) amax_per_head_kernel<128><<<ga, 256, 0, st>>>(src, qc->src_dtype, nslices, Hkv, amax);
+    else amax_per_head_kernel<256><<<ga, 256, 0, st>>>(src, qc->src_dtype, nslices, Hkv, amax); }
     ProfScope ps(kProfQuant, st);
-    e = cudaLaunchCooperativeKernel((const void*)quant_e4m3_kernel, dim3(grid), dim3(256), args, 0, st);
-    if (e != cudaSuccess) return fail(DD_ERR_CUDA, cudaGetErrorString(e));
+    quant_e4m3_kernel<<<grid_for(nelem / 8 / kQuantUnroll, 256), 256, 0, st>>>(
+        src, qc->src_dtype, nelem, Hkv, D, amax, qc->scale_mode, codes,
+        reinterpret_cast<float*>(scales));
   } else {
     ProfScope ps(kProfQuant, st);
     quant_mx_kernel<<<grid_for(nelem / 8 / kQuantUnroll, 256), 256, 0, st>>>(src, qc->src_dtype, nelem, codes,
