@@ -506,21 +506,39 @@ def run_tree(args, world, rank, local, dev):
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # > 126 MB L2
     del q
 
-    def decode(plan_, q_in):
+    coll_ev = []  # (start, end) events around the all-gather + reorder of each step
+
+    def decode(plan_, q_in, evs=None):
         dd.cascade_decode(lcfg, plan_, q_in, kv_local, sc_local, out_local, lse, ws)
         if heads:
+            if evs is not None:
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
             if world > 1:
                 dist.all_gather_into_tensor(gathered, out_local)
             else:
                 gathered[0].copy_(out_local)
             dd.scatter_head_shards(cfg, world, gathered, out)
+            if evs is not None:
+                e1.record()
+                evs.append((e0, e1))
             return out
         return out_local
 
     def step():
-        decode(plan, q_local)
+        decode(plan, q_local, coll_ev if heads else None)
 
     ms_step, launches, clk = timed_steps(step, flush, args, world, rank, local, dev)
+    coll_ms = None
+    if heads:
+        # All-gather + head reorder per timed step (includes waiting for the
+        # slowest rank's attention), max over ranks.
+        timed = coll_ev[-args.steps:]
+        t = torch.tensor([sum(a.elapsed_time(b) for a, b in timed) / max(len(timed), 1)],
+                         dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        coll_ms = float(t.item())
     prof_steps = min(args.steps, 20)
     prof = profile_kernels(step, flush, prof_steps)
 
@@ -578,9 +596,19 @@ def run_tree(args, world, rank, local, dev):
                                np.array(appended[b], np.uint32)]) for b in range(B)]
         return np.concatenate([[0], np.cumsum(lens)]).astype(np.int32), np.concatenate(ids), ntok_e
 
+    # Where an end-to-end step's time goes: device intervals between events on
+    # the stream (query copy, plan upload, decode, output copy) and the host's
+    # planning time, summed over the steps.
+    brk = {"h2d_queries": 0.0, "plan_upload": 0.0, "decode": 0.0, "d2h_output": 0.0,
+           "host_plan": 0.0, "steps": 0}
+
     def e2e_step():
         nonlocal p2
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+        evs[0].record()
         q_dev2.copy_(q_host, non_blocking=True)  # in flight while the host plans
+        evs[1].record()
+        th = time.perf_counter()
         if pb is not None:
             buf = p2.device_buffer
             p2 = make_plan()
@@ -595,10 +623,17 @@ def run_tree(args, world, rank, local, dev):
             ntok_e[:] += 1
             if not p2.advance(ones, new_block):
                 p2.rebuild(*grown_tables())
+        brk["host_plan"] += time.perf_counter() - th
         p2.upload(dev)
+        evs[2].record()
         r = decode(p2, q_dev2)
+        evs[3].record()
         out_host.copy_(r, non_blocking=True)
+        evs[4].record()
         torch.cuda.synchronize()
+        for k, (a, b) in zip(("h2d_queries", "plan_upload", "decode", "d2h_output"), zip(evs, evs[1:])):
+            brk[k] += a.elapsed_time(b) * 1e-3
+        brk["steps"] += 1
         return p2.info().device_bytes
 
     e2e_step_s = e2e_time(e2e_step, args, world, dev)
@@ -641,10 +676,13 @@ def run_tree(args, world, rank, local, dev):
                          "launch_ms": dom["launch_ms"], "algorithmic": dom["algorithmic"]},
             "kernel_rooflines": kernels,
             "kernel_ms_per_step": {k: v[0] / max(prof_steps, 1) for k, v in prof.items() if v[1]},
+            "allgather_ms_per_step": coll_ms,
             "cpu_baseline": cpu,
             "e2e": {"value": total_queries / e2e_step_s, "unit": "queries/s",
                     "h2d_bytes_per_step": int(q_local.numel() * 2 + plan_bytes),
-                    "d2h_bytes_per_step": int(res.numel() * 2), "ms_per_step": e2e_step_s * 1e3},
+                    "d2h_bytes_per_step": int(res.numel() * 2), "ms_per_step": e2e_step_s * 1e3,
+                    "breakdown_ms": {k: round(v / max(brk["steps"], 1) * 1e3, 4) for k, v in brk.items()
+                                     if k != "steps"}},
             "clocks": clk, "gpu_launches": launches,
         }
         print(json.dumps(line), flush=True)

@@ -78,12 +78,63 @@ static int flat_nsplit(const dd_attn_config* c, int32_t B, int32_t max_pages) {
 
 using namespace dd;
 
+namespace dd {
+void release_staging(dd_plan* p) {
+  if (p->staging_event) {
+    cudaEventSynchronize((cudaEvent_t)p->staging_event);
+    cudaEventDestroy((cudaEvent_t)p->staging_event);
+  }
+  if (p->staging) cudaFreeHost(p->staging);
+  p->staging = nullptr;
+  p->staging_event = nullptr;
+  p->staging_bytes = 0;
+  p->staging_device = -1;
+}
+}  // namespace dd
+
 extern "C" int dd_plan_upload(dd_plan* p, void* buf, size_t bytes, dd_stream_t stream) {
   if (!p || !buf) return fail(DD_ERR_INVALID_ARGUMENT, "NULL argument");
   if (bytes < p->image.size()) return fail(DD_ERR_WORKSPACE, "plan device buffer too small");
   if ((uintptr_t)buf & (kAlign - 1)) return fail(DD_ERR_INVALID_ARGUMENT, "plan buffer must be 256-byte aligned");
-  cudaError_t e = cudaMemcpyAsync(buf, p->image.data(), p->image.size(), cudaMemcpyHostToDevice,
-                                  (cudaStream_t)stream);
+  // The image goes through a pinned copy kept by the plan: a copy from
+  // pageable memory would first wait for all work queued on the stream (the
+  // caller's query upload, say) and stall the host. The previous upload's
+  // copy must have left the staging buffer before it is overwritten.
+  const size_t n = p->image.size();
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (p->staging_event && p->staging_device != dev) release_staging(p);
+  if (p->staging_event) cudaEventSynchronize((cudaEvent_t)p->staging_event);
+  if (p->staging_bytes < n) {
+    if (p->staging) cudaFreeHost(p->staging);
+    p->staging = nullptr;
+    p->staging_bytes = 0;
+    const size_t want = n + n / 2;
+    if (cudaHostAlloc(&p->staging, want, cudaHostAllocDefault) == cudaSuccess) {
+      p->staging_bytes = want;
+    } else {
+      cudaGetLastError();
+      p->staging = nullptr;
+    }
+  }
+  if (p->staging && !p->staging_event) {
+    cudaEvent_t ev;
+    if (cudaEventCreateWithFlags(&ev, cudaEventDisableTiming) == cudaSuccess) {
+      p->staging_event = ev;
+      p->staging_device = dev;
+    } else {
+      cudaGetLastError();
+    }
+  }
+  cudaError_t e;
+  if (p->staging && p->staging_event) {
+    std::memcpy(p->staging, p->image.data(), n);
+    e = cudaMemcpyAsync(buf, p->staging, n, cudaMemcpyHostToDevice, (cudaStream_t)stream);
+    if (e == cudaSuccess) e = cudaEventRecord((cudaEvent_t)p->staging_event, (cudaStream_t)stream);
+  } else {
+    // No pinned memory to be had: the plain (stream-ordered, host-blocking) copy.
+    e = cudaMemcpyAsync(buf, p->image.data(), n, cudaMemcpyHostToDevice, (cudaStream_t)stream);
+  }
   if (e != cudaSuccess) return cuda_fail(e, "plan upload");
   p->device_base = buf;
   cudaGetDevice(&p->device_id);

@@ -119,11 +119,19 @@ struct dd_plan {
   // Set by dd_plan_upload.
   const void* device_base = nullptr;
   int device_id = -1;
+  // Pinned host copy of the image for dd_plan_upload (api.cu), so the upload
+  // is a true asynchronous copy, and the event of its last copy.
+  void* staging = nullptr;
+  size_t staging_bytes = 0;
+  void* staging_event = nullptr;
+  int staging_device = -1;
   dd::PlanScratch* scratch = nullptr;
   ~dd_plan();
 };
 
 namespace dd {
+// Frees the plan's pinned upload staging (api.cu).
+void release_staging(dd_plan* p);
 // Thread-local error message used by dd_last_error().
 void set_error(const std::string& msg);
 int fail(int code, const std::string& msg);

@@ -611,7 +611,10 @@ static void pack_image(dd_plan* p) {
 
 }  // namespace dd
 
-dd_plan::~dd_plan() { delete scratch; }
+dd_plan::~dd_plan() {
+  dd::release_staging(this);
+  delete scratch;
+}
 
 using namespace dd;
 

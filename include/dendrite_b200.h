@@ -145,8 +145,7 @@ typedef struct dd_plan_info {
   size_t device_bytes;     /* required size of the buffer given to dd_plan_upload */
   /* Unique KV tokens read by each attention kernel: [0] CUDA-core kernel,
    * [1] streaming tensor-core (mma) kernel, [2] tcgen05 kernel (wide nodes),
-   * [3] tcgen05 kernel on CTA pairs (the widest nodes), [4] tcgen05
-   * streaming kernel (narrow nodes, packed). */
+   * [3] tcgen05 kernel on CTA pairs (the widest nodes), [4] unused (0). */
   int64_t kv_tokens_by_kernel[5];
   /* Sum over tcgen05 nodes and KV heads of (query rows x tokens): the
    * kernel's 4 * head_dim FLOPs per unit (Q.K^T and P.V). */
@@ -201,7 +200,10 @@ int dd_plan_rebuild(dd_plan* plan, int32_t batch_size, const int32_t* block_indp
 int dd_plan_advance(dd_plan* plan, const int32_t* tokens_added, const uint32_t* new_block);
 int dd_plan_get_info(const dd_plan* plan, dd_plan_info* info);
 /* Copies the plan's arrays into caller-owned device memory (>= device_bytes,
- * 256-byte aligned). Must be called before dd_cascade_decode. */
+ * 256-byte aligned). Must be called before dd_cascade_decode. The copy is
+ * asynchronous on `stream`, from a pinned host buffer the plan keeps (grown
+ * with cudaHostAlloc when the plan grows; freed by dd_plan_destroy); the next
+ * upload of the same plan first waits for this copy to finish. */
 int dd_plan_upload(dd_plan* plan, void* device_buf, size_t bytes, dd_stream_t stream);
 /* Host view of the plan's nodes, for tests and tooling. Each array may be
  * NULL; non-NULL arrays have num_nodes entries, except node_pages: every
