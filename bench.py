@@ -602,13 +602,10 @@ def run_tree(args, world, rank, local, dev):
     brk = {"h2d_queries": 0.0, "plan_upload": 0.0, "decode": 0.0, "d2h_output": 0.0,
            "host_plan": 0.0, "steps": 0}
 
-    def e2e_step():
+    def plan_next():
+        """The tree grows one token per leaf: the plan of the next step (the
+        engine knows it before this step's outputs exist)."""
         nonlocal p2
-        evs = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
-        evs[0].record()
-        q_dev2.copy_(q_host, non_blocking=True)  # in flight while the host plans
-        evs[1].record()
-        th = time.perf_counter()
         if pb is not None:
             buf = p2.device_buffer
             p2 = make_plan()
@@ -623,13 +620,23 @@ def run_tree(args, world, rank, local, dev):
             ntok_e[:] += 1
             if not p2.advance(ones, new_block):
                 p2.rebuild(*grown_tables())
-        brk["host_plan"] += time.perf_counter() - th
-        p2.upload(dev)
+
+    def e2e_step():
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+        evs[0].record()
+        q_dev2.copy_(q_host, non_blocking=True)
+        evs[1].record()
+        p2.upload(dev)  # asynchronous, from the plan's pinned staging copy
         evs[2].record()
         r = decode(p2, q_dev2)
         evs[3].record()
         out_host.copy_(r, non_blocking=True)
         evs[4].record()
+        # The next step's plan is made on the host while this step runs on
+        # the device (its upload waits for this step's copy to finish).
+        th = time.perf_counter()
+        plan_next()
+        brk["host_plan"] += time.perf_counter() - th
         torch.cuda.synchronize()
         for k, (a, b) in zip(("h2d_queries", "plan_upload", "decode", "d2h_output"), zip(evs, evs[1:])):
             brk[k] += a.elapsed_time(b) * 1e-3

@@ -100,41 +100,6 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t&
                : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
                : "r"(addr));
 }
-__device__ __forceinline__ void mma_f16(float (&c)[4], const uint32_t (&a)[4], uint32_t b0,
-                                        uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
-      "{%8,%9}, {%0,%1,%2,%3};"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-// MXFP8 in f16: two E4M3 codes -> f16x2 (exact), times a power-of-two pair
-// (exact while the products stay within f16's range, which the E8M0 window
-// below guarantees).
-__device__ __forceinline__ uint32_t e4m3x2_f16x2(uint32_t c2) {
-  const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(c2 & 0xffffu), __NV_E4M3);
-  return (uint32_t)h.x | ((uint32_t)h.y << 16);
-}
-__device__ __forceinline__ uint32_t hmul2_bits(uint32_t a, uint32_t b) {
-  uint32_t d;
-  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-  return d;
-}
-// f16 bits of 2^(e - 127) for an E8M0 byte e in the window [113, 134].
-__device__ __forceinline__ uint32_t e8m0_f16_bits(uint32_t e) { return (e - 112u) << 10; }
-// All four E8M0 bytes of w within [113, 134] (2^-14 .. 2^7): E4M3 codes
-// (|c| <= 448, multiples of 2^-9) times such a scale are exact f16 values.
-__device__ __forceinline__ bool e8m0_f16_window(uint32_t w) {
-  return __vcmpleu4(__vsub4(w, 0x71717171u), 0x15151515u) == 0xffffffffu;
-}
-__device__ __forceinline__ uint32_t bf16x2_to_f16x2(uint32_t w) {
-  const __half2 h = __floats2half2_rn(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
-  return *reinterpret_cast<const uint32_t*>(&h);
-}
-__device__ __forceinline__ bool bf16x2_f16_range(uint32_t w) {  // |both| <= 65280
-  return (w & 0x7fffu) <= 0x477Fu && ((w >> 16) & 0x7fffu) <= 0x477Fu;
-}
-
 __device__ __forceinline__ void mma_bf16(float (&c)[4], const uint32_t (&a)[4], uint32_t b0,
                                          uint32_t b1) {
   asm volatile(
@@ -422,10 +387,6 @@ __global__ void __launch_bounds__(MmaCfg<D, KV>::kThreads, 1)
     uint8_t* qbuf = base + S * C::kStageAll + C::kExpBytes;
     WorkItem it{};
     uint32_t qa[D / 16][4];
-    // MXFP8: Q as f16 too, for the stages whose V and K tiles are f16-exact
-    // (products in f16, P as one f16 term, one P.V product instead of two).
-    uint32_t qa16[KV == kKvMx ? D / 16 : 1][4];
-    bool q16 = false;
     float o[D / 8][4];
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
     float sc_k = 1.f, sc_v = 1.f;  // per-head E4M3 scales of the current item
@@ -462,17 +423,6 @@ __global__ void __launch_bounds__(MmaCfg<D, KV>::kThreads, 1)
             qa[kk][1] = r1.x;
             qa[kk][2] = r0.y;
             qa[kk][3] = r1.y;
-          }
-          if (KV == kKvMx) {
-            bool ok = true;
-#pragma unroll
-            for (int kk = 0; kk < D / 16; ++kk)
-#pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                ok = ok && bf16x2_f16_range(qa[kk][i]);
-                qa16[kk][i] = bf16x2_to_f16x2(qa[kk][i]);
-              }
-            q16 = __all_sync(0xffffffffu, ok);
           }
         }
         __syncwarp();
@@ -529,19 +479,6 @@ __global__ void __launch_bounds__(MmaCfg<D, KV>::kThreads, 1)
             vex[j][i] = *reinterpret_cast<const uint32_t*>(
                 mx + (kStepPages + pj + j) * C::kMxBytes + (2 * (lane & 3) + (i & 1) + 8 * (i >> 1)) * (D / 32));
       }
-      // MXFP8 stage in f16 when every exponent of its K and V lies in the
-      // window and Q fits f16.
-      bool f16s = false;
-      if (KV == kKvMx) {
-        bool ok = q16;
-#pragma unroll
-        for (int nt = 0; nt < (C::kPair ? 2 : 4); ++nt) ok = ok && e8m0_f16_window(kex[nt]);
-#pragma unroll
-        for (int j = 0; j < (C::kPair ? 1 : 2); ++j)
-#pragma unroll
-          for (int i = 0; i < 4; ++i) ok = ok && e8m0_f16_window(vex[j][i]);
-        f16s = __all_sync(0xffffffffu, ok);
-      }
       if (valid[0] + valid[1] > 0) {
         // S = Q K^T for 16 rows x 32 tokens: four independent n-tile chains.
         float sacc[4][4];
@@ -584,24 +521,12 @@ __global__ void __launch_bounds__(MmaCfg<D, KV>::kThreads, 1)
             if (nt >= 2 && !two) break;
             const int odd = ((lane >> 2) & 1);
             const uint4 lo = odd ? ky[nt] : kx[nt], hi = odd ? kx[nt] : ky[nt];
-            const uint32_t wv[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
-            if (KV == kKvMx && f16s) {
-              const uint32_t hl = e8m0_f16_bits((kex[nt] >> (8 * (c >> 1))) & 0xffu);
-              const uint32_t hh = e8m0_f16_bits((kex[nt] >> (8 * (2 + (c >> 1)))) & 0xffu);
-              const uint32_t sl = hl | (hl << 16), sh = hh | (hh << 16);
-#pragma unroll
-              for (int kk = 0; kk < D / 16; ++kk) {
-                const uint32_t sc2 = kk < 4 ? sl : sh;
-                mma_f16(sacc[nt], qa16[KV == kKvMx ? kk : 0], hmul2_bits(e4m3x2_f16x2(wv[kk]), sc2),
-                        hmul2_bits(e4m3x2_f16x2(wv[kk] >> 16), sc2));
-              }
-              continue;
-            }
             float mlo = sc_k, mhi = sc_k;
             if (KV == kKvMx) {
               mlo = e8m0_byte_to_float(kex[nt], c >> 1);
               mhi = e8m0_byte_to_float(kex[nt], 2 + (c >> 1));
             }
+            const uint32_t wv[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
 #pragma unroll
             for (int kk = 0; kk < D / 16; ++kk) {
               uint32_t b0, b1;
@@ -662,43 +587,6 @@ __global__ void __launch_bounds__(MmaCfg<D, KV>::kThreads, 1)
         for (int j = 0; j < 2; ++j) {
           if (j == 1 && !two) break;
           uint32_t pa[4], pl[4];
-          if (KV == kKvMx && f16s) {
-            // P as one f16 term (11 significant bits), V widened to exact f16.
-            uint32_t ph[4];
-            const float2 pp[4] = {make_float2(p[2 * j][0], p[2 * j][1]), make_float2(p[2 * j][2], p[2 * j][3]),
-                                  make_float2(p[2 * j + 1][0], p[2 * j + 1][1]),
-                                  make_float2(p[2 * j + 1][2], p[2 * j + 1][3])};
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const __half2 h = __floats2half2_rn(pp[i].x, pp[i].y);
-              ph[i] = *reinterpret_cast<const uint32_t*>(&h);
-            }
-            const uint8_t* vs = vb + j * C::kSliceRaw;
-            const int g = lane >> 2, c = lane & 3;
-            const int t0 = 2 * c, t1 = 2 * c + 1, t2 = 2 * c + 8, t3 = 2 * c + 9;
-#pragma unroll
-            for (int b = 0; b < D / 32; ++b) {
-              const int off = 4 * (g & 3);
-              const int ch = 2 * b + (g >> 2);
-              const uint32_t w0 = *reinterpret_cast<const uint32_t*>(vs + t0 * D + ((ch ^ (t0 & 7)) << 4) + off);
-              const uint32_t w1 = *reinterpret_cast<const uint32_t*>(vs + t1 * D + ((ch ^ (t1 & 7)) << 4) + off);
-              const uint32_t w2 = *reinterpret_cast<const uint32_t*>(vs + t2 * D + ((ch ^ (t2 & 7)) << 4) + off);
-              const uint32_t w3 = *reinterpret_cast<const uint32_t*>(vs + t3 * D + ((ch ^ (t3 & 7)) << 4) + off);
-              const uint32_t a01 = __byte_perm(w0, w1, 0x5140), b01 = __byte_perm(w0, w1, 0x7362);
-              const uint32_t a23 = __byte_perm(w2, w3, 0x5140), b23 = __byte_perm(w2, w3, 0x7362);
-              const uint32_t u[4] = {__byte_perm(a01, a23, 0x5410), __byte_perm(a01, a23, 0x7632),
-                                     __byte_perm(b01, b23, 0x5410), __byte_perm(b01, b23, 0x7632)};
-              uint32_t h4[4];
-#pragma unroll
-              for (int i = 0; i < 4; ++i) h4[i] = e8m0_f16_bits((vex[j][i] >> (8 * b)) & 0xffu);
-              const uint32_t s01 = h4[0] | (h4[1] << 16), s23 = h4[2] | (h4[3] << 16);
-#pragma unroll
-              for (int d = 0; d < 4; ++d)
-                mma_f16(o[4 * b + d], ph, hmul2_bits(e4m3x2_f16x2(u[d]), s01),
-                        hmul2_bits(e4m3x2_f16x2(u[d] >> 16), s23));
-            }
-            continue;
-          }
           split_bf16x2(p[2 * j][0], p[2 * j][1], pa[0], pl[0]);
           split_bf16x2(p[2 * j][2], p[2 * j][3], pa[1], pl[1]);
           split_bf16x2(p[2 * j + 1][0], p[2 * j + 1][1], pa[2], pl[2]);
