@@ -16,7 +16,7 @@ int launch_attn_mma(const AttnArgs& a, int64_t num_pages, cudaStream_t st, bool 
 bool mma_supported(int D, int kv_dtype);
 int launch_attn_tc(const AttnArgs& a, int64_t num_pages, int grid, cudaStream_t st);
 int launch_attn_tc2(const AttnArgs& a, int64_t num_pages, int num_items, cudaStream_t st);
-cudaError_t launch_merge(const MergeArgs& a, cudaStream_t st, bool after_stream);
+cudaError_t launch_merge(const MergeArgs& a, cudaStream_t st);
 
 static int cuda_fail(cudaError_t e, const char* what) {
   return fail(DD_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
@@ -217,8 +217,7 @@ extern "C" int dd_cascade_decode(const dd_attn_config* cfg, const dd_plan* p, co
   m.Hq = cfg->num_qo_heads;
   m.D = cfg->head_dim;
   m.out_dtype = cfg->q_dtype;
-  const bool merge_pdl = !prof_timing_on() && (!p->items[kItemMma].empty());
-  e = launch_merge(m, st, merge_pdl);
+  e = launch_merge(m, st);
   if (e != cudaSuccess) return cuda_fail(e, "merge launch");
   return DD_OK;
 }
@@ -283,7 +282,7 @@ extern "C" int dd_decode_paged(const dd_attn_config* cfg, int32_t B, int32_t max
   m.Hq = cfg->num_qo_heads;
   m.D = cfg->head_dim;
   m.out_dtype = cfg->q_dtype;
-  e = launch_merge(m, st, false);
+  e = launch_merge(m, st);
   if (e != cudaSuccess) return cuda_fail(e, "merge launch");
   return DD_OK;
 }

@@ -717,10 +717,6 @@ __global__ void __launch_bounds__(MmaCfg<D, KV>::kThreads, 1)
       }
     }
   }
-  // This CTA has no work left: a merge launched as this grid's programmatic
-  // dependent may be dispatched (it waits for this grid's completion before
-  // reading any partial state).
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   // Launched as a programmatic dependent of the tcgen05 kernel (cascade
   // decode), this grid starts while that one runs, on the SMs it leaves free
   // and on each SM it gives up; it completes only after it, so the merge that

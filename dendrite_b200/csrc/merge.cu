@@ -21,10 +21,7 @@ __global__ void __launch_bounds__(256) merge_paths_kernel(MergeArgs a) {
   constexpr int E = D / 32;
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  if (warp >= a.batch * a.Hq) {
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-    return;
-  }
+  if (warp >= a.batch * a.Hq) return;
   const int p = warp / a.Hq, h = warp % a.Hq;
   int n;
   int32_t base = 0;
@@ -37,20 +34,12 @@ __global__ void __launch_bounds__(256) merge_paths_kernel(MergeArgs a) {
   float M = -INFINITY, W = 0.f, acc[E];
 #pragma unroll
   for (int e = 0; e < E; ++e) acc[e] = 0.f;
-  auto slot_of = [&](int i) -> int64_t {
-    return a.path_indptr ? (int64_t)a.path_slots[base + i] + h : ((int64_t)i * a.batch + p) * a.Hq + h;
-  };
-  // The plan's slot ids are read before waiting for the attention kernels
-  // (a programmatic dependent launch starts this grid early); their partial
-  // states only after.
-  int64_t slot0 = lane < n ? slot_of(lane) : 0;
-  asm volatile("griddepcontrol.wait;" ::: "memory");
   for (int c0 = 0; c0 < n; c0 += 32) {
     const int i = c0 + lane;
     int64_t slot = 0;
     float l = -INFINITY;
     if (i < n) {
-      slot = c0 == 0 ? slot0 : slot_of(i);
+      slot = a.path_indptr ? (int64_t)a.path_slots[base + i] + h : ((int64_t)i * a.batch + p) * a.Hq + h;
       l = a.part_lse[slot];
     }
     float cm = l;
@@ -99,30 +88,17 @@ __global__ void __launch_bounds__(256) merge_paths_kernel(MergeArgs a) {
     a.lse[(size_t)q * a.Hq + h] = W > 0.f ? (M + log2f(W)) * kLn2 : -INFINITY;
 }
 
-cudaError_t launch_merge(const MergeArgs& a, cudaStream_t st, bool after_stream) {
+cudaError_t launch_merge(const MergeArgs& a, cudaStream_t st) {
   const int64_t warps = (int64_t)a.batch * a.Hq;
   if (warps == 0) return cudaSuccess;
   const int blocks = (int)((warps * 32 + 255) / 256);
   ProfScope ps(kProfMerge, st);
-  cudaLaunchConfig_t lc = {};
-  lc.gridDim = dim3(blocks);
-  lc.blockDim = dim3(256);
-  lc.stream = st;
-  cudaLaunchAttribute attr[1];
-  if (after_stream) {
-    // Programmatic dependent of the streaming kernel, whose CTAs signal as
-    // they run out of work: this grid's launch and its reads of the plan
-    // overlap that kernel's tail.
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    lc.attrs = attr;
-    lc.numAttrs = 1;
-  }
   switch (a.D) {
-    case 64: return cudaLaunchKernelEx(&lc, merge_paths_kernel<64>, a);
-    case 128: return cudaLaunchKernelEx(&lc, merge_paths_kernel<128>, a);
-    default: return cudaLaunchKernelEx(&lc, merge_paths_kernel<256>, a);
+    case 64: merge_paths_kernel<64><<<blocks, 256, 0, st>>>(a); break;
+    case 128: merge_paths_kernel<128><<<blocks, 256, 0, st>>>(a); break;
+    default: merge_paths_kernel<256><<<blocks, 256, 0, st>>>(a); break;
   }
+  return cudaGetLastError();
 }
 
 // Element-wise two-state merge in the natural-log convention of
