@@ -21,13 +21,14 @@
 //               sub-tile while the softmax of the other runs (ping-pong).
 //   warps 2-9   softmax, one thread per row: warps 2-5 own sub-tile A, 6-9
 //               sub-tile B (a warp may only touch the TMEM lanes of its
-//               quarter, warp % 4). Per tile: row max (pass 1), then per
-//               64-token chunk exp2, row sum and P as two bf16 terms (hi +
-//               lo: P.V keeps ~16 significant bits of P) written over the
-//               chunk's own scores (pass 2). The running max is used lazily:
-//               O and the sum are rescaled only when the row max grows by
-//               more than 2^8, otherwise the exponentials keep the stale max,
-//               which is exact.
+//               quarter, warp % 4). One pass per 64-token chunk: its max,
+//               exp2, row sum and P as two bf16 terms (hi + lo: P.V keeps
+//               ~16 significant bits of P) written over the chunk's own
+//               scores. The exponentials use a running integer reference
+//               that moves only when a chunk's max passes it by more than 16
+//               (log2 units); then O, the sum and the tile's earlier P are
+//               scaled by the exact power of two, otherwise the stale
+//               reference is kept, which is exact.
 // TMEM columns: A: S/P 0-127, O 128-255; B: S/P 256-383, O 384-511. P_j
 // overwrites S_j in place: S_{j+1} is committed after P.V_j, so when the
 // softmax sees S_{j+1} the previous P has been consumed and O is final for
@@ -410,8 +411,16 @@ __global__ void __launch_bounds__(TcCfg<KV>::kThreads, 1)
         const int valid = min((j == ntiles - 1) ? (npages - kTcPagesPerTile * j - 1) * kPageSize + it.last_valid
                                                 : kTcTok,
                               row_lim == INT_MAX ? kTcTok : max(row_lim - kTcTok * j, 0));
-        // Pass 1: row max of the raw scores (the scale is positive).
-        float mx = -INFINITY;
+        // One pass per 64-token chunk: the exponentials use the running
+        // reference m_used (an integer, in log2 units), which moves only
+        // when a chunk's max exceeds it by more than 16 (the first chunk of
+        // the first tile always; later, practically never). Then O, the row
+        // sum and the P this tile already holds are scaled by the exact power
+        // of two 2^(m_used - m_new). P.V_{j-1} is complete here (S_j was
+        // committed after it), so O can be rescaled in place; tcgen05.ld/st
+        // are warp-wide, hence the warp-uniform decision (a factor of 1
+        // leaves a row as is).
+        const uint64_t sc2 = f2_pack(scale_log2, scale_log2);
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
           float s[64];
@@ -437,46 +446,17 @@ __global__ void __launch_bounds__(TcCfg<KV>::kThreads, 1)
             m0 = max3f(m0, s[i], s[i + 1]);
             m1 = max3f(m1, s[i + 2], s[i + 3]);
           }
-          mx = max3f(mx, max3f(m0, m1, s[62]), s[63]);
-        }
-        float mt = mx * scale_log2;
-        if (!ok) mt = m_used;
-        // Lazy rescale: the exponentials use a stale max unless the row max
-        // grew by more than 2^8. P.V_{j-1} is complete here (S_j was committed
-        // after it), so O can be rescaled in place; tcgen05.ld/st are warp-wide,
-        // hence the warp-uniform decision (a factor of 1 leaves a row as is).
-        if (__any_sync(0xffffffffu, mt > m_used + kRescaleThreshold)) {
-          const float m_new = fmaxf(m_used, mt);
-          const float f = fast_exp2(m_used - m_new);  // 0 when m_used is -inf
-          if (j > 0) {
-#pragma unroll
-            for (int c = 0; c < 4; ++c) tmem_scale32(o_col + c * 32, f);
+          // Raw scores times a positive scale: the max commutes.
+          const float mt = ok ? max3f(m0, m1, fmaxf(s[62], s[63])) * scale_log2 : m_used;
+          if (__any_sync(0xffffffffu, mt > m_used + kTcRescaleThreshold)) {
+            const float m_new = mt > m_used + kTcRescaleThreshold ? ceilf(mt) : m_used;
+            const float f = exp2f(m_used - m_new);  // a power of two; 0 when m_used is -inf
+            if (j > 0) tmem_scale_cols<false>(o_col, 128, f);
+            if (c == 1) tmem_scale_cols<true>(s_col, 64, f);  // chunk 0's P (hi, lo terms)
+            lsum = f2_fma(lsum, f2_pack(f, f), 0ull);
+            m_used = m_new;
           }
-          lsum = f2_fma(lsum, f2_pack(f, f), 0ull);
-          m_used = m_new;
-        }
-        // Pass 2: exponentials, sum, P (hi, lo) over each chunk's own scores.
-        const uint64_t sc2 = f2_pack(scale_log2, scale_log2), nm2 = f2_pack(-m_used, -m_used);
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          float s[64];
-          {
-            float t[32];
-            tmem_ld32(s_col + c * 64, t);
-#pragma unroll
-            for (int i = 0; i < 32; ++i) s[i] = t[i];
-            tmem_ld32(s_col + c * 64 + 32, t);
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) s[32 + i] = t[i];
-          }
-          const int vc = valid - c * 64;
-          if (vc < 64) {
-#pragma unroll
-            for (int i = 0; i < 64; ++i)
-              if (i >= vc) s[i] = -INFINITY;
-          }
-          softmax_chunk(s, sc2, nm2, lsum, s_col + c * 64);
+          softmax_chunk(s, sc2, f2_pack(-m_used, -m_used), lsum, s_col + c * 64);
         }
         tmem_wait_st();
         tc_fence_before();

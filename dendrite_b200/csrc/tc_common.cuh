@@ -16,7 +16,8 @@ constexpr uint32_t kTmemCols = 512;
 // Per sub-tile x: S (then P over it) at col_s(x), O at col_o(x).
 __device__ __forceinline__ uint32_t col_s(int x) { return (uint32_t)x * 256u; }
 __device__ __forceinline__ uint32_t col_o(int x) { return (uint32_t)x * 256u + 128u; }
-constexpr float kRescaleThreshold = 8.0f;  // log2 units
+constexpr float kRescaleThreshold = 8.0f;  // log2 units (attn_tc2.cu)
+constexpr float kTcRescaleThreshold = 16.0f;  // log2 units (attn_tc.cu, single pass)
 
 // Instruction descriptors, kind::f16, D f32, A/B bf16, M = 128, N = 128.
 constexpr uint32_t kIdescQK = (1u << 4) | (1u << 7) | (1u << 10) | ((128u >> 3) << 17) |
@@ -107,6 +108,35 @@ __device__ __forceinline__ void tmem_scale32(uint32_t taddr, float f) {
     o[i + 1] = f2_hi(v);
   }
   tmem_st32(taddr, o);
+}
+
+__device__ __forceinline__ void tmem_ld16u(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+      "%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+// `cols` columns (a multiple of 16) at taddr of this thread's lane, times f,
+// 16 columns at a time: as f32 values, or (bf16x2) as two bf16 values each.
+// With f a power of two the products are exact (within the formats' normal
+// ranges). The rare rescale of the single-pass softmax; kept narrow so it
+// needs few registers next to a live chunk of scores.
+template <bool kBf16x2>
+__device__ __noinline__ void tmem_scale_cols(uint32_t taddr, int cols, float f) {
+  for (int c = 0; c < cols; c += 16) {
+    uint32_t v[16];
+    tmem_ld16u(taddr + c, v);
+    tmem_wait_ld();
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+      v[i] = kBf16x2 ? pack_bf16x2(__uint_as_float(v[i] << 16) * f, __uint_as_float(v[i] & 0xffff0000u) * f)
+                     : __float_as_uint(__uint_as_float(v[i]) * f);
+    tmem_st16u(taddr + c, v);
+  }
+  tmem_wait_st();
 }
 
 // Softmax of one 64-token chunk (s[], scores already masked): P = exp2(s *
