@@ -124,6 +124,26 @@ def test_large_score_range_rescales(cuda):
     np.testing.assert_allclose(lse, ref_lse, rtol=1e-4, atol=1e-2)
 
 
+def test_score_jump_inside_a_tile(cuda):
+    """A page of very large keys in the second 64-token chunk of the first
+    tile and another in a later tile: the single-pass softmax moves its
+    reference mid-tile and rescales the P it already wrote, O and the sum."""
+    indptr, ids, ntok, P = _groups([(40, 1024)], 6)
+    tb = _TB(32, 8, 128, indptr, ids, ntok, P)
+    rng = np.random.default_rng(6)
+    x = random_pool(rng, P, 8, 128)
+    order = ids[:ntok[0] // 16]
+    x[order[5], 0] *= 40.0    # tile 0, chunk 1 (tokens 80-95)
+    x[order[37], 0] *= 80.0   # tile 4
+    pool = bf16_bits(x)
+    q = bf16_bits(rng.standard_normal((len(ntok), 32, 128)).astype(np.float32))
+    got, lse, prof, _ = _run(tb, pool, q, cuda)
+    assert prof["attn_tc"][1] >= 1
+    ref, ref_lse = oracle.decode_batch(bits_to_f32(q), pool, indptr, ids, ntok, 8)
+    assert_close(got, bits_to_f32(bf16_bits(ref)), what="score jump")
+    np.testing.assert_allclose(lse, ref_lse, rtol=1e-4, atol=1e-2)
+
+
 @pytest.mark.parametrize("pairs", [False, True])
 def test_mcts_subset_vs_oracle(cuda, pairs):
     """A 128-leaf version of the MCTS tree (root through tcgen05), all queries."""
