@@ -320,24 +320,28 @@ __global__ void append_kv_kernel(void* kv, int dtype, uint32_t page, int slot0, 
   }
 }
 
+// One 16-byte chunk per thread and step: rows of D elements are contiguous
+// on both sides, so the head-shard reorder is a gather of 16-byte vectors.
 __global__ void scatter_heads_kernel(int world, int B, int Hq, int Hkv, int D, int gqa_map,
                                      int dtype, const void* gathered, void* out) {
   const int Hq_r = Hq / world, Hkv_r = Hkv / world, g = Hq / Hkv;
-  const int64_t n = (int64_t)world * B * Hq_r * D;
+  const int cpr = D * (dtype == DD_DTYPE_F32 ? 4 : 2) / 16;  // chunks per row
+  const int64_t rows = (int64_t)world * B * Hq_r;
+  const int64_t n = rows * cpr;
+  const uint4* src = reinterpret_cast<const uint4*>(gathered);
+  uint4* dst = reinterpret_cast<uint4*>(out);
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
-    const int d = (int)(i % D);
-    const int li = (int)((i / D) % Hq_r);
-    const int b = (int)((i / ((int64_t)D * Hq_r)) % B);
-    const int r = (int)(i / ((int64_t)D * Hq_r * B));
+    const int64_t row = i / cpr;
+    const int c = (int)(i - row * cpr);
+    const int li = (int)(row % Hq_r);
+    const int64_t rb = row / Hq_r;
+    const int b = (int)(rb % B);
+    const int r = (int)(rb / B);
     const int k0 = r * Hkv_r;
     // Local head li of rank r -> global query head (same GQA layout locally).
     const int h = gqa_map == DD_GQA_TILED ? (k0 + li % Hkv_r) + (li / Hkv_r) * Hkv : k0 * g + li;
-    const size_t dst = ((size_t)b * Hq + h) * D + d;
-    if (dtype == DD_DTYPE_F32)
-      reinterpret_cast<float*>(out)[dst] = reinterpret_cast<const float*>(gathered)[i];
-    else
-      reinterpret_cast<uint16_t*>(out)[dst] = reinterpret_cast<const uint16_t*>(gathered)[i];
+    dst[((int64_t)b * Hq + h) * cpr + c] = src[i];
   }
 }
 }  // namespace dd
@@ -373,7 +377,9 @@ extern "C" int dd_scatter_head_shards(const dd_attn_config* cfg, int32_t world, 
   if (B < 0) return fail(DD_ERR_INVALID_ARGUMENT, "bad batch size");
   if (B == 0) return DD_OK;
   if (!gathered || !out) return fail(DD_ERR_INVALID_ARGUMENT, "NULL pointer");
-  const int64_t n = (int64_t)B * cfg->num_qo_heads * cfg->head_dim;
+  if (((uintptr_t)gathered & 15) || ((uintptr_t)out & 15))
+    return fail(DD_ERR_INVALID_ARGUMENT, "gathered / out must be 16-byte aligned");
+  const int64_t n = (int64_t)B * cfg->num_qo_heads * cfg->head_dim * (cfg->q_dtype == DD_DTYPE_F32 ? 4 : 2) / 16;
   const int blocks = (int)std::min<int64_t>((n + 255) / 256, 4096);
   ProfScope ps(kProfOther, (cudaStream_t)stream);
   scatter_heads_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(

@@ -374,7 +374,8 @@ int dd_dequantize_kv_pages(const dd_quant_config* qc, const uint8_t* codes,
 /* Multi-GPU helper for the KV-head split of one long tree: after an
  * all-gather of per-rank outputs gathered[rank][batch][Hq/world][D], writes
  * out[batch][Hq][D]. rank r owns KV heads [r*Hkv/world, (r+1)*Hkv/world) and
- * the query heads that map to them under cfg->gqa_map. */
+ * the query heads that map to them under cfg->gqa_map. Both buffers must be
+ * 16-byte aligned (rows move as 16-byte vectors). */
 int dd_scatter_head_shards(const dd_attn_config* cfg, int32_t world, int32_t batch_size,
                            const void* gathered, void* out, dd_stream_t stream);
 
