@@ -508,7 +508,31 @@ def run_tree(args, world, rank, local, dev):
 
     coll_ev = []  # (start, end) events around the all-gather + reorder of each step
 
+    fused = hs.FusedHeadSplit(cfg, world, rank, B, dev) if heads and args.join == "p2p" else None
+
     def decode(plan_, q_in, evs=None):
+        if fused is not None:
+            # The join fused into the merge (NVLink stores into every rank's
+            # output); the events bracket the cross-rank barrier after it.
+            if plan_.device_buffer is None:
+                plan_.upload(dev)
+            from dendrite_b200.backend import _ptr, _stream
+            import ctypes as C
+            h = fused.handles[fused.step % 2]
+            _lib.check(_lib.lib.dd_cascade_decode_shards(
+                C.byref(lcfg), plan_._h, _ptr(q_in), _ptr(kv_local), _ptr(sc_local),
+                C.c_void_p(int(h.buffer_ptrs_dev)), world, rank, cfg.num_qo_heads, cfg.num_kv_heads,
+                _ptr(lse), _ptr(ws), ws.numel(), _stream(None)), "dd_cascade_decode_shards")
+            if evs is not None:
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+            h.barrier(channel=0)
+            if evs is not None:
+                e1.record()
+                evs.append((e0, e1))
+            r = fused.bufs[fused.step % 2]
+            fused.step += 1
+            return r
         dd.cascade_decode(lcfg, plan_, q_in, kv_local, sc_local, out_local, lse, ws)
         if heads:
             if evs is not None:
@@ -674,7 +698,7 @@ def run_tree(args, world, rank, local, dev):
                        "unique_kv_tokens_per_rank": info.kv_tokens,
                        "flat_kv_tokens_per_rank": info.kv_tokens_flat, "plan_nodes": info.num_nodes, "tc_ctas": info.tc_ctas,
                        "l2": "flushed between steps (256 MiB write, untimed)",
-                       "parallelism": f"{w['split']} x{world}"},
+                       "parallelism": f"{w['split']} x{world}" + (f", join {args.join}" if heads else "")},
             "effective_gbs": gbs, "hbm_frac": gbs / (hbm_peak * world),
             "roofline": {"bound": dom["bound"], "kernel": attn_kind, "achieved": dom["achieved"],
                          "peak": dom["peak"], "unit": dom["unit"], "frac": dom["frac"],
@@ -793,6 +817,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="mcts8b")
     ap.add_argument("--cpu-budget", type=float, default=10.0)
+    ap.add_argument("--join", choices=["nccl", "p2p"], default="nccl",
+                    help="long70b: join the head shards by NCCL all-gather + reorder, or inside "
+                         "the merge by NVLink stores into symmetric memory (dd_cascade_decode_shards)")
     ap.add_argument("--tc-sms", type=int, default=0,
                     help="CTAs of the tcgen05 kernel (plan option tc_sms: 0 = one per SM, "
                          "-1 = one CTA per work item)")

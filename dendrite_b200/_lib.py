@@ -106,6 +106,8 @@ SIGNATURES = {
     "dd_plan_export_nodes": (C.c_int, [_VP, _I32P, _I32P, _I32P, _I32P, _I32P, _I32P, _U32P,
                                        _I32P]),
     "dd_cascade_decode": (C.c_int, [_CFGP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, C.c_size_t, _VP]),
+    "dd_cascade_decode_shards": (C.c_int, [_CFGP, _VP, _VP, _VP, _VP, _VP, C.c_int32, C.c_int32,
+                                           C.c_int32, C.c_int32, _VP, _VP, C.c_size_t, _VP]),
     "dd_decode_paged_workspace_size": (C.c_size_t, [_CFGP, C.c_int32, C.c_int32]),
     "dd_decode_paged": (C.c_int, [_CFGP, C.c_int32, C.c_int32, _VP, _VP, _VP, _VP, _VP, _VP,
                                   _VP, _VP, _VP, C.c_size_t, _VP]),

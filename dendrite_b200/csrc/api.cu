@@ -141,9 +141,44 @@ extern "C" int dd_plan_upload(dd_plan* p, void* buf, size_t bytes, dd_stream_t s
   return DD_OK;
 }
 
+// Rank placement of a head-split decode whose merge writes into peer memory.
+struct PeerOut {
+  void* const* ptrs;
+  int32_t world, rank, Hq_global, Hkv_global;
+};
+
+static int cascade_decode_impl(const dd_attn_config* cfg, const dd_plan* p, const void* q,
+                               const void* kv, const void* scales, void* out, float* lse,
+                               void* ws, size_t ws_bytes, dd_stream_t stream, const PeerOut* po);
+
 extern "C" int dd_cascade_decode(const dd_attn_config* cfg, const dd_plan* p, const void* q,
                                  const void* kv, const void* scales, void* out, float* lse,
                                  void* ws, size_t ws_bytes, dd_stream_t stream) {
+  return cascade_decode_impl(cfg, p, q, kv, scales, out, lse, ws, ws_bytes, stream, nullptr);
+}
+
+extern "C" int dd_cascade_decode_shards(const dd_attn_config* cfg_local, const dd_plan* p,
+                                        const void* q_local, const void* kv_local,
+                                        const void* scales_local, void* const* peer_out,
+                                        int32_t world, int32_t rank, int32_t num_qo_heads,
+                                        int32_t num_kv_heads, float* lse_local, void* ws,
+                                        size_t ws_bytes, dd_stream_t stream) {
+  int rc = check_config(cfg_local);
+  if (rc) return rc;
+  if (!peer_out) return fail(DD_ERR_INVALID_ARGUMENT, "peer_out is NULL");
+  if (world < 1 || rank < 0 || rank >= world) return fail(DD_ERR_INVALID_ARGUMENT, "bad world / rank");
+  if (num_kv_heads != cfg_local->num_kv_heads * world || num_qo_heads != cfg_local->num_qo_heads * world)
+    return fail(DD_ERR_INVALID_ARGUMENT, "global head counts must be the local ones times world");
+  const PeerOut po{peer_out, world, rank, num_qo_heads, num_kv_heads};
+  // The local output buffer is not written; q_local stands in for the
+  // pointer checks.
+  return cascade_decode_impl(cfg_local, p, q_local, kv_local, scales_local,
+                             const_cast<void*>(q_local), lse_local, ws, ws_bytes, stream, &po);
+}
+
+static int cascade_decode_impl(const dd_attn_config* cfg, const dd_plan* p, const void* q,
+                               const void* kv, const void* scales, void* out, float* lse,
+                               void* ws, size_t ws_bytes, dd_stream_t stream, const PeerOut* po) {
   int rc = check_config(cfg);
   if (rc) return rc;
   if (!p) return fail(DD_ERR_INVALID_ARGUMENT, "plan is NULL");
@@ -217,6 +252,14 @@ extern "C" int dd_cascade_decode(const dd_attn_config* cfg, const dd_plan* p, co
   m.Hq = cfg->num_qo_heads;
   m.D = cfg->head_dim;
   m.out_dtype = cfg->q_dtype;
+  if (po) {
+    m.peer_out = po->ptrs;
+    m.world = po->world;
+    m.rank = po->rank;
+    m.Hq_global = po->Hq_global;
+    m.Hkv_global = po->Hkv_global;
+    m.gqa_map = cfg->gqa_map;
+  }
   e = launch_merge(m, st);
   if (e != cudaSuccess) return cuda_fail(e, "merge launch");
   return DD_OK;

@@ -397,6 +397,11 @@ struct MergeArgs {
   void* out;
   float* lse;
   int32_t batch, Hq, D, out_dtype;
+  // Head-split decode with the outputs written straight into every rank's
+  // output buffer (peer memory): peer_out[world] device pointers to
+  // [batch][Hq_global][D]; this rank's local head h goes to its global head.
+  void* const* peer_out = nullptr;
+  int32_t world = 1, rank = 0, Hq_global = 0, Hkv_global = 0, gqa_map = 0;
 };
 
 }  // namespace dd

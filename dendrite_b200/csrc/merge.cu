@@ -75,7 +75,25 @@ __global__ void __launch_bounds__(256) merge_paths_kernel(MergeArgs a) {
   const int q = a.qorder ? a.qorder[p] : p;
   const size_t ob = ((size_t)q * a.Hq + h) * D + lane * E;
   const float inv = W > 0.f ? 1.f / W : 0.f;
-  if (a.out_dtype == DD_DTYPE_F32) {
+  if (a.peer_out) {
+    // Head split: the row goes to its global head in every rank's output
+    // (NVLink stores into peer memory; local head h of rank r under the
+    // GQA map restricted to the rank's KV heads).
+    const int Hkv_r = a.Hkv_global / a.world, k0 = a.rank * Hkv_r, g = a.Hq_global / a.Hkv_global;
+    const int hg = a.gqa_map == DD_GQA_TILED ? (k0 + h % Hkv_r) + (h / Hkv_r) * a.Hkv_global : k0 * g + h;
+    const size_t og = ((size_t)q * a.Hq_global + hg) * D + lane * E;
+    for (int r = 0; r < a.world; ++r) {
+      if (a.out_dtype == DD_DTYPE_F32) {
+#pragma unroll
+        for (int e = 0; e < E; ++e) reinterpret_cast<float*>(a.peer_out[r])[og + e] = acc[e] * inv;
+      } else {
+#pragma unroll
+        for (int e = 0; e < E; e += 2)
+          *reinterpret_cast<uint32_t*>(reinterpret_cast<__nv_bfloat16*>(a.peer_out[r]) + og + e) =
+              pack_bf16x2(acc[e] * inv, acc[e + 1] * inv);
+      }
+    }
+  } else if (a.out_dtype == DD_DTYPE_F32) {
 #pragma unroll
     for (int e = 0; e < E; ++e) reinterpret_cast<float*>(a.out)[ob + e] = acc[e] * inv;
   } else {

@@ -123,3 +123,53 @@ def allgather_heads(nccl_comm: int, cfg: AttnConfig, world: int, local_out: torc
                                            _stream(stream)), "dd_allgather_heads")
     return out
 
+
+
+class FusedHeadSplit:
+    """The head split with the join fused into the decode
+    (dd_cascade_decode_shards): the final merge of every rank writes its rows
+    straight into all ranks' output buffers over NVLink, so no all-gather and
+    no reorder kernel run. The outputs live in symmetric memory (torch's
+    CUDA-backend allocation, mapped into every rank), two buffers used in
+    turn; after each decode the ranks meet at a device-side barrier, so the
+    returned buffer is complete, and a buffer is written again only after
+    every rank has passed the next step's barrier (by then each rank has
+    consumed it in stream order)."""
+
+    def __init__(self, cfg: AttnConfig, world: int, rank: int, batch_size: int, device,
+                 group=None):
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm
+
+        self.cfg, self.world, self.rank = cfg, world, rank
+        self.lcfg = shard_config(cfg, world)
+        if symm.get_backend(device) is None:
+            symm.set_backend("CUDA")
+        g = group if group is not None else dist.group.WORLD
+        dtype = torch.bfloat16 if cfg.q_dtype == _lib.DTYPE_BF16 else torch.float32
+        self.bufs, self.handles = [], []
+        for _ in range(2):
+            t = symm.empty((batch_size, cfg.num_qo_heads, cfg.head_dim), dtype=dtype, device=device)
+            self.bufs.append(t)
+            self.handles.append(symm.rendezvous(t, g))
+        self.step = 0
+
+    def decode(self, plan_local: CascadePlan, q_local: torch.Tensor, kv_local: torch.Tensor,
+               scales_local: torch.Tensor | None, lse_local: torch.Tensor,
+               workspace: torch.Tensor, stream=None) -> torch.Tensor:
+        import ctypes as C
+
+        from .backend import _ptr, _stream
+
+        i = self.step % 2
+        h = self.handles[i]
+        if plan_local.device_buffer is None:
+            plan_local.upload(q_local.device, stream)
+        _lib.check(_lib.lib.dd_cascade_decode_shards(
+            C.byref(self.lcfg), plan_local._h, _ptr(q_local), _ptr(kv_local), _ptr(scales_local),
+            C.c_void_p(int(h.buffer_ptrs_dev)), self.world, self.rank, self.cfg.num_qo_heads,
+            self.cfg.num_kv_heads, _ptr(lse_local), _ptr(workspace), workspace.numel(),
+            _stream(stream)), "dd_cascade_decode_shards")
+        h.barrier(channel=0)
+        self.step += 1
+        return self.bufs[i]

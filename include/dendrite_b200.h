@@ -371,6 +371,25 @@ int dd_dequantize_kv_pages(const dd_quant_config* qc, const uint8_t* codes,
                            const void* scales, int64_t num_pages, void* dst,
                            int32_t dst_dtype, dd_stream_t stream);
 
+/* KV-head split of one long tree with the join fused into the decode: as
+ * dd_cascade_decode on this rank's shard (cfg_local = Hq/world query heads
+ * over Hkv/world KV heads, plan built with cfg_local, q_local / kv_local /
+ * scales_local the rank's heads as dd_scatter_head_shards documents), but the
+ * final merge writes each output row at its global head of EVERY rank's
+ * output [batch][num_qo_heads][head_dim]: peer_out is a DEVICE array of
+ * `world` device pointers to those buffers (peer memory mapped into this
+ * process, e.g. a symmetric-memory allocation; NVLink stores, no collective
+ * library). lse_local [batch][Hq/world] stays local. The caller synchronises
+ * the ranks after the call (before reading the output) and before a rank's
+ * next call can overwrite a buffer another rank still reads. Replaces the
+ * decode + NCCL all-gather + reorder of the head split; no reference
+ * counterpart (the reference runs no multi-GPU attention). */
+int dd_cascade_decode_shards(const dd_attn_config* cfg_local, const dd_plan* plan,
+                             const void* q_local, const void* kv_local, const void* scales_local,
+                             void* const* peer_out, int32_t world, int32_t rank,
+                             int32_t num_qo_heads, int32_t num_kv_heads, float* lse_local,
+                             void* workspace, size_t workspace_bytes, dd_stream_t stream);
+
 /* Multi-GPU helper for the KV-head split of one long tree: after an
  * all-gather of per-rank outputs gathered[rank][batch][Hq/world][D], writes
  * out[batch][Hq][D]. rank r owns KV heads [r*Hkv/world, (r+1)*Hkv/world) and

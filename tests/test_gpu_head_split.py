@@ -4,9 +4,12 @@
   shards stacked as an all-gather would, reordered by dd_scatter_head_shards,
   and compared with the oracle over all heads.
 * dd_allgather_heads through a one-rank NCCL communicator on one GPU.
+* dd_cascade_decode_shards (the join fused into the merge) with W = 1, 2, 4
+  emulated on one GPU.
 * With two or more GPUs, two processes (one per GPU) join their shards with
-  dd_allgather_heads over NCCL and with head_split_decode over
-  torch.distributed; both must match the oracle.
+  dd_allgather_heads over NCCL, with head_split_decode over
+  torch.distributed, and with FusedHeadSplit (NVLink stores into symmetric
+  memory); all must match the oracle.
 """
 import ctypes as C
 import os
@@ -62,6 +65,44 @@ def test_emulated_split_vs_oracle(cuda, world, gqa):
     dd.scatter_head_shards(cfg, world, gathered.contiguous(), out)
     torch.cuda.synchronize()
     assert_close(out.float().cpu().numpy(), ref, what=f"split x{world}")
+
+
+def _shards_call(tb, cfg, pool_d, q_d, rank, world, outs, dev):
+    """dd_cascade_decode_shards of one rank, writing into every buffer of `outs`."""
+    from dendrite_b200.backend import _ptr
+
+    lcfg = hs.shard_config(cfg, world)
+    plan = dd.CascadePlan(lcfg, tb.indptr, tb.block_ids, tb.num_tokens)
+    plan.upload(dev)
+    ws = torch.empty(max(int(plan.info().workspace_bytes), 256), dtype=torch.uint8, device=dev)
+    lse = torch.empty(tb.batch_size, HQ // world, dtype=torch.float32, device=dev)
+    ptrs = torch.tensor([o.data_ptr() for o in outs], dtype=torch.int64, device=dev)
+    _lib.check(_lib.lib.dd_cascade_decode_shards(
+        C.byref(lcfg), plan._h, _ptr(hs.shard_queries(q_d, cfg, rank, world)),
+        _ptr(hs.shard_pages(pool_d, rank, world)), None, C.c_void_p(ptrs.data_ptr()), world, rank,
+        HQ, HKV, _ptr(lse), _ptr(ws), ws.numel(), None), "dd_cascade_decode_shards")
+    torch.cuda.synchronize()
+
+
+@pytest.mark.parametrize("world", [1, 2, 4])
+@pytest.mark.parametrize("gqa", [_lib.GQA_TILED, _lib.GQA_GROUPED])
+def test_shards_entry_emulated(cuda, world, gqa):
+    """dd_cascade_decode_shards with W ranks emulated on one GPU: each rank's
+    merge writes its rows into all W output buffers (here all local), which
+    must each end up equal to the reordered all-gather result, and the oracle."""
+    tb, pool, q, ref = _problem(gqa)
+    cfg = dd.make_config(HQ, HKV, D, tb.num_pages, gqa_map=gqa)
+    pool_d, q_d = _dev(pool, cuda), _dev(q, cuda)
+    outs = [torch.full_like(q_d, float("nan")) for _ in range(world)]
+    for r in range(world):
+        _shards_call(tb, cfg, pool_d, q_d, r, world, outs, cuda)
+    gathered = torch.stack([_shard_out(tb, cfg, pool_d, q_d, r, world, cuda) for r in range(world)])
+    want = torch.empty_like(q_d)
+    dd.scatter_head_shards(cfg, world, gathered.contiguous(), want)
+    torch.cuda.synchronize()
+    for o in outs:
+        assert torch.equal(o, want)
+    assert_close(outs[0].float().cpu().numpy(), ref, what=f"shards x{world}")
 
 
 def _nccl():
@@ -122,6 +163,16 @@ def _two_gpu_rank(rank, world, idfile, port, result):
             b = hs.head_split_decode(cfg, plan, hs.shard_queries(q_d, cfg, rank, world),
                                      hs.shard_pages(pool_d, rank, world), None, world)
             torch.cuda.synchronize()
+            # The fused join: every rank's merge writes into both ranks'
+            # symmetric-memory outputs; three steps (both buffers, reused).
+            fh = hs.FusedHeadSplit(cfg, world, rank, tb.batch_size, dev)
+            ws = torch.empty(max(int(plan.info().workspace_bytes), 256), dtype=torch.uint8, device=dev)
+            lse = torch.empty(tb.batch_size, HQ // world, dtype=torch.float32, device=dev)
+            for _ in range(3):
+                c = fh.decode(plan, hs.shard_queries(q_d, cfg, rank, world),
+                              hs.shard_pages(pool_d, rank, world), None, lse, ws)
+                torch.cuda.synchronize()
+                assert torch.equal(c, b)
             assert torch.equal(a, b)
             assert_close(a.float().cpu().numpy(), ref, what=f"2 GPUs gqa={gqa}")
         result[rank] = "ok"
