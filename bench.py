@@ -13,14 +13,18 @@ Other workloads (--workload):
                               trees partitioned across the ranks
   long70b                     config 5b: one tree, 131072-token prefix + 256 x
                               256-token branches, split by KV-head group across
-                              the ranks with an all-gather of the head outputs
+                              the ranks; the head outputs are joined inside the
+                              merge by NVLink stores into every rank's output
+                              (--join p2p, default) or by an NCCL all-gather +
+                              reorder (--join nccl)
   quant-e4m3, quant-mxfp8     config 2: quantize a 4096-page x [2][4][16][64]
                               bf16 pool (67.1 MB) with 0.1% x50 outliers
 
 Multi-GPU (torchrun, one process per GPU): mcts8b* give every rank its own
 tree (no collective; weak scaling); forest70b splits the 64 trees over the
 ranks (strong scaling, no collective); long70b splits the KV heads (strong
-scaling, one NCCL all-gather per step inside the timed region). `value` is
+scaling; the join and a cross-rank barrier, or an NCCL all-gather, inside
+the timed region of every step). `value` is
 the whole job's queries (or bytes) per second over the max-over-ranks time.
 
 Output: one JSON line (rank 0). `--impl reference` times the reference's CPU
@@ -817,7 +821,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="mcts8b")
     ap.add_argument("--cpu-budget", type=float, default=10.0)
-    ap.add_argument("--join", choices=["nccl", "p2p"], default="nccl",
+    ap.add_argument("--join", choices=["nccl", "p2p"], default="p2p",
                     help="long70b: join the head shards by NCCL all-gather + reorder, or inside "
                          "the merge by NVLink stores into symmetric memory (dd_cascade_decode_shards)")
     ap.add_argument("--tc-sms", type=int, default=0,
