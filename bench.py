@@ -15,8 +15,9 @@ Other workloads (--workload):
                               256-token branches, split by KV-head group across
                               the ranks; the head outputs are joined inside the
                               merge by NVLink stores into every rank's output
-                              (--join p2p, default) or by an NCCL all-gather +
-                              reorder (--join nccl)
+                              (--join p2p; the default up to 2 ranks) or by an
+                              NCCL all-gather + reorder (--join nccl; the
+                              default beyond)
   quant-e4m3, quant-mxfp8     config 2: quantize a 4096-page x [2][4][16][64]
                               bf16 pool (67.1 MB) with 0.1% x50 outliers
 
@@ -512,7 +513,8 @@ def run_tree(args, world, rank, local, dev):
 
     coll_ev = []  # (start, end) events around the all-gather + reorder of each step
 
-    fused = hs.FusedHeadSplit(cfg, world, rank, B, dev) if heads and args.join == "p2p" else None
+    join = args.join if args.join != "auto" else ("p2p" if world <= 2 else "nccl")
+    fused = hs.FusedHeadSplit(cfg, world, rank, B, dev) if heads and join == "p2p" else None
 
     def decode(plan_, q_in, evs=None):
         if fused is not None:
@@ -702,7 +704,7 @@ def run_tree(args, world, rank, local, dev):
                        "unique_kv_tokens_per_rank": info.kv_tokens,
                        "flat_kv_tokens_per_rank": info.kv_tokens_flat, "plan_nodes": info.num_nodes, "tc_ctas": info.tc_ctas,
                        "l2": "flushed between steps (256 MiB write, untimed)",
-                       "parallelism": f"{w['split']} x{world}" + (f", join {args.join}" if heads else "")},
+                       "parallelism": f"{w['split']} x{world}" + (f", join {join}" if heads else "")},
             "effective_gbs": gbs, "hbm_frac": gbs / (hbm_peak * world),
             "roofline": {"bound": dom["bound"], "kernel": attn_kind, "achieved": dom["achieved"],
                          "peak": dom["peak"], "unit": dom["unit"], "frac": dom["frac"],
@@ -821,9 +823,10 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="mcts8b")
     ap.add_argument("--cpu-budget", type=float, default=10.0)
-    ap.add_argument("--join", choices=["nccl", "p2p"], default="p2p",
+    ap.add_argument("--join", choices=["auto", "nccl", "p2p"], default="auto",
                     help="long70b: join the head shards by NCCL all-gather + reorder, or inside "
-                         "the merge by NVLink stores into symmetric memory (dd_cascade_decode_shards)")
+                         "the merge by NVLink stores into symmetric memory (dd_cascade_decode_shards); "
+                         "auto: p2p up to 2 ranks, NCCL beyond (measured faster at 8)")
     ap.add_argument("--tc-sms", type=int, default=0,
                     help="CTAs of the tcgen05 kernel (plan option tc_sms: 0 = one per SM, "
                          "-1 = one CTA per work item)")
