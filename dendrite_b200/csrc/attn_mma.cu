@@ -44,15 +44,6 @@
 namespace dd {
 
 constexpr int kMmaRows = 16;       // query rows per work item
-#ifndef DD_MMA_BF16_PAIR
-#define DD_MMA_BF16_PAIR 0
-#endif
-#ifndef DD_MMA_BF16_STREAMS
-#define DD_MMA_BF16_STREAMS 4
-#endif
-#ifndef DD_MMA_BF16_STAGES
-#define DD_MMA_BF16_STAGES 3
-#endif
 constexpr int kStepPages = 2;      // pages per stage
 constexpr int kItemSlots = 2;      // item descriptors per stream
 
@@ -65,9 +56,12 @@ struct MmaCfg {
   static constexpr int kMxBytes = KV == kKvMx ? kPageSize * (D / 32) : 0;
   // Stages are read in place by the consumer; FP8 stages are a quarter (E4M3)
   // of the bf16 ones, so the FP8 rings are deeper for the same bytes in flight.
-  static constexpr bool kPair = KV != kKvBf16 || (D == 128 && DD_MMA_BF16_PAIR);
-  static constexpr int kStreams = KV == kKvBf16 ? DD_MMA_BF16_STREAMS : 4;  // independent streams per CTA
-  static constexpr int kStages = KV == kKvBf16 ? DD_MMA_BF16_STAGES : 5;
+  // bf16 streams have one consumer warp (consumer pairs for bf16, with 2
+  // stages of 4 streams or 3 stages of 3 streams to fit shared memory,
+  // measured slower: 142-146 us against 133 us on config 3).
+  static constexpr bool kPair = KV != kKvBf16;
+  static constexpr int kStreams = 4;  // independent streams per CTA
+  static constexpr int kStages = KV == kKvBf16 ? 3 : 5;
   static constexpr int kRawStage = 2 * kStepPages * kSliceRaw;         // K0 K1 V0 V1
   static constexpr int kMxStage = 2 * kStepPages * kMxBytes;
   static constexpr int kStageAll = kRawStage;                          // 1 KiB multiple (swizzle)
