@@ -193,3 +193,24 @@ def test_rebuild_matches_fresh_plan():
     with pytest.raises(dd.InvalidArgument):
         live.rebuild(trees[0].indptr, bad, trees[0].num_tokens)
     assert live.info().batch_size == 0 and live.info().num_items == 0
+
+
+def test_tcgen05_schedule_sizes():
+    """The tcgen05 work items go onto one CTA per SM at most (or the CTAs the
+    tc_sms option asks for); tc_sms = -1 keeps one CTA per item; the
+    makespan-aware split keeps config 5a's 32768-token roots whole."""
+    tb = wl.mcts_llama3_8b(0xD3D1)
+    cfg = dd.make_config(32, 8, 128, tb.num_pages)
+    auto = dd.CascadePlan(cfg, tb.indptr, tb.block_ids, tb.num_tokens).info()
+    per_item = dd.CascadePlan(cfg, tb.indptr, tb.block_ids, tb.num_tokens, tc_sms=-1).info()
+    fixed = dd.CascadePlan(cfg, tb.indptr, tb.block_ids, tb.num_tokens, tc_sms=60).info()
+    assert auto.tc_ctas == 148
+    assert fixed.tc_ctas == 60
+    assert per_item.tc_ctas > 148  # one CTA per item, more items than SMs
+    forest = wl.llama3_70b_forest(num_trees=8, seed=1)
+    fcfg = dd.make_config(64, 8, 128, forest.num_pages)
+    f_auto = dd.CascadePlan(fcfg, forest.indptr, forest.block_ids, forest.num_tokens).info()
+    f_item = dd.CascadePlan(fcfg, forest.indptr, forest.block_ids, forest.num_tokens, tc_sms=-1).info()
+    # 8 trees x 2 row tiles x 8 KV heads = 128 unsplit root items; the older
+    # rule cut them further, the schedule keeps them whole.
+    assert f_auto.workspace_bytes < f_item.workspace_bytes
